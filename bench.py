@@ -1,0 +1,489 @@
+#!/usr/bin/env python
+"""bench.py -- W4A16 decode GEMV throughput on B200 (the BASELINE metric).
+
+Metric: achieved HBM read GB/s (and % of the measured B200 read roof) and
+µs per GEMV, 4096x4096, batch 1.
+
+A *step* is one decode-style pass over a stack of ``sets`` distinct
+4096x4096 int4 weight matrices (64 by default, 555 MB in total, > 4x the
+126 MB L2), one batch-1 GEMV per matrix.  Every byte of every matrix is read
+from HBM once per step -- no L2 flush is needed because no matrix is touched
+again until 63 others have streamed through L2.
+
+value   device-resident throughput: the step is captured once in a CUDA
+        graph (GEMVs launched through the C ABI with programmatic dependent
+        launch, so each kernel's weight stream overlaps its predecessor's
+        tail) and replayed K times between CUDA events.
+e2e     the same metric through the public Python API (decode_kernel.gemv,
+        the reference's operator surface): per step, the step's activations
+        come from pinned host memory and the outputs go back to the host.
+cpu_baseline / --impl reference
+        the reference's CPU path (fp32 dequantize-then-matmul,
+        python/decode_kernel/reference.py:17-26) restated in numpy
+        (oracle/oracle.py: linear_fp32_np), timed on the host cores.
+
+Multi-GPU (torchrun, one rank per GPU): each rank streams its own weight
+stack (weak scaling, no data-path collective); time = max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "decode-kernel_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = ("achieved HBM read GB/s (% of measured B200 read roof) and µs/GEMV, "
+          "4096x4096 B=1")
+L2_BYTES = 126 * 1024 * 1024
+
+
+def gemv_bytes(m: int, k: int, b: int) -> int:
+    """Algorithmic bytes of one GEMV: packed W + scales + x + y
+    (bench/common.py:111-117 of the reference)."""
+    return m * (k // 2) + m * (k // 128) * 2 + b * k * 2 + b * m * 2
+
+
+# --------------------------------------------------------------------------
+# helpers
+# --------------------------------------------------------------------------
+
+def dist_info():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic_per_launch():
+    """dram read+write bytes per launch of the dominant kernel, from the
+    committed ncu summary (profiles/), or None."""
+    p = REPO / "profiles" / "k_stream_4096x4096_b1.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except Exception:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (recipe's clocks line)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), parts[3], parts[4:]))
+                except ValueError:
+                    continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for name, val in zip(names[1:], r[3][1:]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows),
+                "reasons": sorted(reasons)}
+
+
+def read_roof_gbs(torch, capi, nbytes=512 << 20, iters=20) -> float:
+    """This library's sm_100a stream_read over 512 MiB: the read-only HBM
+    roof the BASELINE metric is quoted against (median of ``iters``)."""
+    src = torch.ones(nbytes // 4, dtype=torch.float32, device="cuda")
+    blocks = capi.load().dk_stream_recommended_blocks(-1)
+    part = torch.empty(blocks, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for i in range(iters + 3):
+        e0.record()
+        capi.check(capi.load().dk_stream_read(src.data_ptr(), part.data_ptr(), nbytes, blocks,
+                                              stream), "dk_stream_read")
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            ts.append(e0.elapsed_time(e1) / 1e3)
+    del src, part
+    return nbytes / statistics.median(ts) / 1e9
+
+
+# --------------------------------------------------------------------------
+# CPU reference path (oracle port) -- reference arm and cpu_baseline
+# --------------------------------------------------------------------------
+
+def cpu_problem(M, K, B, seed=0):
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02)
+    x = rng.standard_normal((B, K), dtype=np.float32).astype(np.float16)
+    packed, scales = O.quantize_and_pack_np(w)
+    return packed, scales, x
+
+
+def time_cpu_reference(M, K, B, budget_s, seed=0):
+    """Times the restated reference CPU path on row samples; returns
+    (GB/s, seconds per sample, rows per sample, samples)."""
+    from oracle import oracle as O
+
+    packed, scales, x = cpu_problem(M, K, B, seed)
+    t0 = time.perf_counter()
+    O.linear_fp32_np(x, packed, scales)
+    t_full = time.perf_counter() - t0
+    n = max(3, min(200, int(budget_s / max(t_full, 1e-3))))
+    ts = []
+    for _ in range(n):
+        t0 = time.perf_counter()
+        O.linear_fp32_np(x, packed, scales)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    return gemv_bytes(M, K, B) / t / 1e9, t, M, n
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_info()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle as O
+
+    M, K, B = args.m, args.k, args.batch
+    packed, scales, x = cpu_problem(M, K, B)
+    # Size each step's row sample so warm-up + K steps take about 90 s.
+    t0 = time.perf_counter()
+    O.linear_fp32_np(x, packed, scales)
+    t_full = time.perf_counter() - t0
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = int(min(M, max(64, (M * budget / t_full) // 64 * 64)))
+    p_s, s_s = np.ascontiguousarray(packed[:rows]), np.ascontiguousarray(scales[:rows])
+    for _ in range(args.warmup):
+        O.linear_fp32_np(x, p_s, s_s)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.linear_fp32_np(x, p_s, s_s)
+    dt = time.perf_counter() - t0
+    gbs = args.steps * gemv_bytes(rows, K, B) / dt / 1e9
+    cores = O.cpu_threads()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": gbs,
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"{M}x{K} W4A16 GEMV B={B}", "M": M, "K": K, "global_batch": B,
+                   "parallelism": "host cores (rank 0 only)"},
+        "cpu_baseline": {
+            "value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"each step: rows [0, {rows}) of the {M}x{K} matrix, x [{B},{K}]; "
+                      f"fp32 dequantize then fp32 BLAS matmul (numpy restatement of "
+                      f"reference.py:17-26), {cores} BLAS threads"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU path
+# --------------------------------------------------------------------------
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+
+    import decode_kernel as dk
+    from decode_kernel import capi
+    from decode_kernel.quantize import quantize_and_pack_cuda
+
+    ws, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+
+    M, K, B, S = args.m, args.k, args.batch, args.sets
+    per_gemv = gemv_bytes(M, K, B)
+    assert S * M * K // 2 > 2 * L2_BYTES, "weight stack must exceed 2x L2"
+
+    # Seeded synthetic weights, quantized on the GPU (bit-exact with the CPU
+    # quantizer), distinct per set and per rank.
+    packed, scales, xs, ys = [], [], [], []
+    for s in range(S):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + s)
+        w = torch.randn(M, K, generator=g, device=dev) * 0.02
+        p, sc = quantize_and_pack_cuda(w)
+        packed.append(p)
+        scales.append(sc)
+        xs.append(torch.randn(B, K, generator=g, device=dev).half())
+        ys.append(torch.empty(B, M, dtype=torch.float16, device=dev))
+        del w
+    torch.cuda.synchronize()
+
+    cfg = capi.default_config(flags=0 if args.no_pdl else capi.DK_FLAG_PDL)
+    lib = capi.load()
+
+    def step(stream):
+        for s in range(S):
+            st = capi.gemv(packed[s].data_ptr(), scales[s].data_ptr(), xs[s].data_ptr(),
+                           ys[s].data_ptr(), M, K, B, cfg, 0, 0, stream)
+            if st:
+                capi.check(st, "dk_w4a16_gemv")
+
+    # Warm-up (eager), then capture one step in a CUDA graph.
+    cur = torch.cuda.current_stream().cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        step(cur)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # Correctness spot check of the measured configuration (first set, 64 rows).
+    if rank == 0:
+        from oracle import oracle as O
+
+        pk = packed[0][:64].cpu().numpy()
+        sc = scales[0][:64].cpu().view(torch.int16).numpy().view(np.uint16)
+        xx = xs[0].cpu().view(torch.int16).numpy().view(np.uint16)
+        ref = O.linear_fp32(xx, pk, sc)
+        err = float(np.abs(ys[0][:, :64].float().cpu().numpy() - ref).max())
+        assert err < 1e-2, f"bench spot check failed: {err}"
+
+    # ---- timed region: K graph replays ----
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t_local = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(t_local, op=pg.ReduceOp.MAX)
+    ms_max = float(t_local.item())
+    launches = args.steps * S
+    value = ws * launches * per_gemv / (ms_max / 1e3) / 1e9
+    us_per_gemv_local = ms * 1e3 / launches
+    achieved = per_gemv / (us_per_gemv_local / 1e6) / 1e9
+    assert lib.dk_device_error(-1, 0) == 0, "a bounded device wait timed out"
+    del graph
+
+    # ---- e2e through the public API with host buffers ----
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    hx = torch.empty((S, B, K), dtype=torch.float16).pin_memory()
+    hx.copy_(torch.stack([x.cpu() for x in xs]))
+    hy = torch.empty((S, B, M), dtype=torch.float16).pin_memory()
+    dx = torch.empty((S, B, K), dtype=torch.float16, device=dev)
+    dy = torch.empty((S, B, M), dtype=torch.float16, device=dev)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        for s in range(S):
+            dy[s].copy_(dk.gemv(packed[s], scales[s], dx[s]))
+        hy.copy_(dy, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(e2e_ms, op=pg.ReduceOp.MAX)
+    e2e_value = ws * e2e_steps * S * per_gemv / (float(e2e_ms.item()) / 1e3) / 1e9
+
+    roof = read_roof_gbs(torch, capi) if rank == 0 else None
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        gbs, t, rows, n = time_cpu_reference(M, K, B, budget_s=args.cpu_budget)
+        cpu = {"value": gbs, "unit": "GB/s", "cores": O.cpu_threads(), "kind": "port",
+               "sample": f"{n} full {M}x{K} B={B} GEMVs (median {t * 1e3:.1f} ms each); fp32 "
+                         f"dequantize then fp32 BLAS matmul (numpy restatement of "
+                         f"reference.py:17-26)"}
+
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    traffic = ncu_traffic_per_launch()
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "us_per_gemv": ms_max * 1e3 / launches,
+        "pct_of_read_roof": (100.0 * value / ws / roof) if roof else None,
+        "read_roof_gbs": roof,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4*f16->f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"{M}x{K} W4A16 GEMV B={B}",
+            "M": M, "K": K, "global_batch": B * ws,
+            "gemvs_per_step": S,
+            "weight_stack_bytes": S * M * K // 2,
+            "l2": f"inputs larger than L2: {S} distinct weight sets "
+                  f"({S * per_gemv / 2**20:.0f} MiB) cycled, no flush",
+            "kernel": "k_stream (v5), PDL" if not args.no_pdl else "k_stream (v5)",
+            "launch": "CUDA graph of one step, replayed",
+            "parallelism": f"weak x{ws}: independent weight stacks per GPU, no collective",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if peak_kind ==
+            "measured" else "fallback 6650 GB/s",
+            "traffic": traffic,
+            "bytes_per_launch": per_gemv,
+        },
+        "e2e": {"value": e2e_value, "unit": "GB/s",
+                "h2d_bytes_per_step": S * B * K * 2, "d2h_bytes_per_step": S * B * M * 2,
+                "steps": e2e_steps,
+                "path": "decode_kernel.gemv (torch extension -> C ABI), pinned host x/y"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--sets", type=int, default=64)
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

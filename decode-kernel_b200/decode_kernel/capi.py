@@ -1,0 +1,112 @@
+"""ctypes binding of the C ABI (include/dk_w4a16.h) in libdk_b200.so.
+
+This is the binding a non-torch caller would write; the tests use it to drive
+the kernels through the exact extern "C" entry points.  Device memory is passed
+as raw addresses (e.g. ``tensor.data_ptr()``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libdk_b200.so"
+
+DK_OK = 0
+DK_ERR_INVALID_ARG = 1
+DK_ERR_UNSUPPORTED = 2
+DK_ERR_LAUNCH = 3
+DK_ERR_TIMEOUT = 4
+DK_ERR_CUDA = 5
+DK_ERR_WORKSPACE = 6
+
+DK_FLAG_PDL = 0x1
+DK_QUANT_TORCH_CUDA_SCALE = 0x1
+
+
+class GemvConfig(ctypes.Structure):
+    """struct dk_gemv_config (gemv_w4a16.h:22-27 GemvLaunchConfig + flags)."""
+
+    _fields_ = [
+        ("version", ctypes.c_int),
+        ("split_k", ctypes.c_int),
+        ("reuse_weights", ctypes.c_int),
+        ("warps_per_row", ctypes.c_int),
+        ("flags", ctypes.c_uint),
+    ]
+
+
+# name -> (restype, argtypes); every symbol include/dk_w4a16.h declares.
+_P, _I, _U, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_size_t
+SIGNATURES = {
+    "dk_gemv_config_init": (None, [ctypes.POINTER(GemvConfig)]),
+    "dk_w4a16_workspace_bytes": (_SZ, [_I, _I, _I, ctypes.POINTER(GemvConfig)]),
+    "dk_w4a16_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, _SZ, _P]),
+    "dk_d2d_copy": (_I, [_P, _P, _SZ, _P]),
+    "dk_stream_read": (_I, [_P, _P, _SZ, _I, _P]),
+    "dk_stream_write": (_I, [_P, _SZ, _I, _P]),
+    "dk_stream_recommended_blocks": (_I, [_I]),
+    "dk_last_kernel_stamp": (_I, [_I]),
+    "dk_device_error": (_I, [_I, _I]),
+    "dk_quantize_pack": (_I, [_P, _I, _I, _P, _P, _U, _P]),
+    "dk_unpack_to_int": (_I, [_P, _I, _I, _P, _P]),
+    "dk_dequantize": (_I, [_P, _P, _I, _I, _P, _P]),
+    "dk_status_string": (ctypes.c_char_p, [_I]),
+    "dk_last_cuda_error": (ctypes.c_char_p, []),
+    "dk_version": (ctypes.c_char_p, []),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libdk_b200.so and attach the declared signatures.  Raises when the
+    library has not been built -- there is nothing to fall back to."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build()")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def default_config(**kw) -> GemvConfig:
+    cfg = GemvConfig()
+    load().dk_gemv_config_init(ctypes.byref(cfg))
+    for k, v in kw.items():
+        setattr(cfg, k, int(v))
+    return cfg
+
+
+class DkError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        lib = load()
+        msg = f"{what}: {lib.dk_status_string(status).decode()}"
+        if status in (DK_ERR_LAUNCH, DK_ERR_CUDA):
+            msg += f" [{lib.dk_last_cuda_error().decode()}]"
+        super().__init__(msg)
+        self.status = status
+
+
+def check(status: int, what: str) -> None:
+    if status != DK_OK:
+        raise DkError(status, what)
+
+
+def gemv(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, M: int, K: int, B: int,
+         cfg: GemvConfig | None = None, workspace_ptr: int = 0, workspace_bytes: int = 0,
+         stream: int = 0) -> int:
+    """dk_w4a16_gemv; returns the status (0 = DK_OK)."""
+    return load().dk_w4a16_gemv(packed_ptr, scales_ptr, x_ptr, y_ptr, M, K, B,
+                                ctypes.byref(cfg) if cfg is not None else None,
+                                workspace_ptr or None, workspace_bytes, stream or None)
+
+
+def workspace_bytes(M: int, K: int, B: int, cfg: GemvConfig | None = None) -> int:
+    return int(load().dk_w4a16_workspace_bytes(M, K, B,
+                                               ctypes.byref(cfg) if cfg is not None else None))

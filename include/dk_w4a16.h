@@ -1,0 +1,150 @@
+/*
+ * dk_w4a16.h -- C ABI of the B200 (sm_100a) W4A16 decode-GEMV library.
+ *
+ * This is the drop-in boundary for RohanDisa/decode-kernel's GEMV path.  The
+ * reference exposes it as C++ functions in namespace decode_kernel
+ * (include/decode_kernel/gemv_w4a16.h) bound to Python by a torch extension
+ * (csrc/bindings.cpp).  Here the same operations are plain extern "C"
+ * functions over raw pointers and sizes -- no torch or C++ types -- so any
+ * FFI (ctypes, cffi, cgo, JNI) can bind them; this repository's torch
+ * extension `decode_kernel._cuda` is one such caller.
+ *
+ * Data format (gemv_w4a16.h:29-33, python/decode_kernel/quantize.py:1-15):
+ *   packed  int32   [M, K/8]   8 signed 4-bit values per word, value k%8 at
+ *                               bits 4*(k%8) (low nibble first), two's
+ *                               complement.
+ *   scales  fp16    [M, K/128] one scale per 128 consecutive k of a row.
+ *   x       fp16    [B, K]
+ *   y       fp16    [B, M]     y[b,m] = sum_k x[b,k] * q[m,k] * scale[m,k/128]
+ * All matrices are row-major and contiguous.  fp16 values are passed as their
+ * IEEE binary16 bit patterns (uint16_t).  K must be a multiple of 128.
+ * `packed` and `x` must be 16-byte aligned (any fresh cudaMalloc/torch
+ * allocation is).
+ *
+ * Streams are cudaStream_t passed as void* (NULL = legacy default stream).
+ * Every call is asynchronous on that stream, allocates nothing, and returns a
+ * status; device-side faults surface on the stream as usual.
+ */
+#ifndef DK_W4A16_H_
+#define DK_W4A16_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DK_API __attribute__((visibility("default")))
+#else
+#define DK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* gemv_w4a16.h:9-11 (kGroupSize, kNibblesPerWord, kWeightsPerInt4). */
+#define DK_GROUP_SIZE 128
+#define DK_NIBBLES_PER_WORD 8
+#define DK_WEIGHTS_PER_INT4 32
+
+/* Status of every call.  The reference prints launch errors and carries on
+ * (gemv_w4a16.cu:9-16); this ABI reports them. */
+typedef enum dk_status {
+  DK_OK = 0,
+  DK_ERR_INVALID_ARG = 1,  /* shape, range or alignment rejected */
+  DK_ERR_UNSUPPORTED = 2,  /* valid request this build cannot serve */
+  DK_ERR_LAUNCH = 3,       /* cudaLaunch* failed; see dk_last_cuda_error() */
+  DK_ERR_TIMEOUT = 4,      /* a bounded device wait ran out */
+  DK_ERR_CUDA = 5,         /* another CUDA runtime call failed */
+  DK_ERR_WORKSPACE = 6     /* workspace missing or smaller than required */
+} dk_status;
+
+/* gemv_w4a16.h:13-20 KernelVersion: the six entries of the reference's kernel
+ * family, each served by its own sm_100a kernel here. */
+typedef enum dk_kernel_version {
+  DK_V0_ROW_SCALAR = 0,   /* one thread per row */
+  DK_V1_WARP_ROW = 1,     /* one warp (or block) per row, CUDA cores */
+  DK_V2_TILE_DIRECT = 2,  /* 16-row tensor-core tiles, 128-bit register loads */
+  DK_V3_TILE_SCALES = 3,  /* v2 with the tile's scales staged in shared memory */
+  DK_V4_SPLIT_K = 4,      /* v2 split along K across CTAs, fp32 workspace */
+  DK_V5_STREAM = 5        /* persistent bulk-copy pipeline (default, fastest) */
+} dk_kernel_version;
+
+/* Launch flags (no counterpart in the reference). */
+#define DK_FLAG_PDL 0x1u /* launch with programmatic stream serialisation: the
+                          * kernel may start while the previous kernel on the
+                          * stream drains and streams its WEIGHTS before waiting
+                          * for it; x and y are touched only after the wait.
+                          * Only valid when the previous kernel on the stream
+                          * does not write `packed` or `scales`. */
+
+/* gemv_w4a16.h:22-27 GemvLaunchConfig, same fields and defaults, plus flags. */
+typedef struct dk_gemv_config {
+  int version;       /* 0..5, default 5 */
+  int split_k;       /* 1..32, default 4; version 4 only */
+  int reuse_weights; /* default 0; non-zero selects the batch weight-reuse path */
+  int warps_per_row; /* 1..8, default 1; >1 only with version 1, no reuse */
+  unsigned flags;    /* DK_FLAG_* */
+} dk_gemv_config;
+
+/* Fills the reference defaults (version 5, split_k 4, no reuse, 1 warp/row). */
+DK_API void dk_gemv_config_init(dk_gemv_config* cfg);
+
+/* Bytes of workspace dk_w4a16_gemv needs for this shape and config (0 when
+ * none).  Replaces the binding's per-call torch::zeros({B,M}) fp32 workspace
+ * (bindings.cpp:63-68); contents need no initialisation. */
+DK_API size_t dk_w4a16_workspace_bytes(int M, int K, int B, const dk_gemv_config* cfg);
+
+/* y = x . dequant(W)^T.  Replaces decode_kernel::w4a16_gemv
+ * (gemv_w4a16.h:34-36, gemv_w4a16.cu:568-591) together with the argument
+ * checks of bindings.cpp:10-48.  M, B == 0 is a no-op; K == 0 writes zeros.
+ * cfg may be NULL (defaults). */
+DK_API dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales, const uint16_t* x,
+                        uint16_t* y, int M, int K, int B, const dk_gemv_config* cfg,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* STREAM-style HBM probes (gemv_w4a16.h:39-43).  `bytes` must be a multiple
+ * of 16 and the pointers 16-byte aligned.  dk_stream_read writes one float
+ * partial sum per block (blocks <= 0 picks dk_stream_recommended_blocks). */
+DK_API dk_status dk_d2d_copy(const void* src, void* dst, size_t bytes, void* stream);
+DK_API dk_status dk_stream_read(const void* src, float* partials, size_t bytes, int blocks,
+                         void* stream);
+DK_API dk_status dk_stream_write(void* dst, size_t bytes, int blocks, void* stream);
+/* gemv_w4a16.cu:602-609, but for the given device (-1 = current) instead of
+ * always device 0. */
+DK_API int dk_stream_recommended_blocks(int device);
+
+/* Stamp written by the GEMV kernel that ran last on `device` (-1 = current):
+ * 0..5 for versions 0..5, 10+w for version 1 with w>1 warps per row, 15 for
+ * the batch weight-reuse path; -1 if none has run.  Synchronises the device
+ * first, like gemv_w4a16.cu:559-564. */
+DK_API int dk_last_kernel_stamp(int device);
+
+/* Device-side error word of `device` (-1 = current): 0, or 1 when a bounded
+ * wait inside a kernel ran out.  Synchronises the device; clears the word
+ * when `clear` is non-zero.  (No counterpart in the reference.) */
+DK_API int dk_device_error(int device, int clear);
+
+/* Format helpers on the GPU, bit-exact with python/decode_kernel/quantize.py
+ * run on the CPU: quantize_and_pack (:26-51), unpack_to_int (:54-63),
+ * dequantize (:66-78).  w is fp32 [M, K]; q is int32 [M, K]. */
+#define DK_QUANT_TORCH_CUDA_SCALE 0x1u /* amax * fp32(1/7) instead of amax / 7,
+                                        * which is what the same torch code
+                                        * computes on a CUDA tensor */
+DK_API dk_status dk_quantize_pack(const float* w, int M, int K, int32_t* packed, uint16_t* scales,
+                           unsigned flags, void* stream);
+DK_API dk_status dk_unpack_to_int(const int32_t* packed, int M, int K, int32_t* q, void* stream);
+DK_API dk_status dk_dequantize(const int32_t* packed, const uint16_t* scales, int M, int K, float* w,
+                        void* stream);
+
+/* Human-readable text for a status; the CUDA error behind the last
+ * DK_ERR_LAUNCH / DK_ERR_CUDA on this thread. */
+DK_API const char* dk_status_string(dk_status s);
+DK_API const char* dk_last_cuda_error(void);
+/* Library version and the architecture it was compiled for ("sm_100a"). */
+DK_API const char* dk_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* DK_W4A16_H_ */

@@ -1,0 +1,198 @@
+"""GPU parity of every GEMV kernel, called through the C ABI (dk_w4a16_gemv),
+against the CPU oracle: max-abs < 1e-2, plus the
+bit-level properties the kernel family guarantees (one canonical reduction
+order for v2/v3/v4/v5/reuse, batch- and row-invariance)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from dkhelpers import MAX_ABS, capi_gemv, make_problem, max_err, oracle_y, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def cfg(**kw):
+    from decode_kernel import capi
+
+    return capi.default_config(**kw)
+
+
+def stamp():
+    from decode_kernel import capi
+
+    return capi.load().dk_last_kernel_stamp(-1)
+
+
+SHAPES = [(256, 256), (64, 128), (48, 384), (33, 1024), (1, 128), (17, 4096), (300, 640),
+          (1000, 2048), (4096, 4096)]
+
+
+@pytest.mark.parametrize("version", [0, 1, 2, 3, 4, 5])
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("batch", [1, 4])
+def test_versions_vs_oracle(version, shape, batch, cuda_device):
+    M, K = shape
+    packed, scales, x = make_problem(M, K, batch, seed=1000 + M + K + batch, std=0.05)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = capi_gemv(tp, ts, tx, cfg(version=version, split_k=4))
+    assert max_err(y, ref) < MAX_ABS
+    assert stamp() == version
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 7, 8, 9, 16, 17, 31, 32, 33, 40, 64])
+@pytest.mark.parametrize("reuse", [0, 1])
+def test_batch_path_vs_oracle(batch, reuse, cuda_device):
+    M, K = 200, 1536
+    packed, scales, x = make_problem(M, K, batch, seed=77 + batch)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = capi_gemv(tp, ts, tx, cfg(version=5, reuse_weights=reuse))
+    assert max_err(y, ref) < MAX_ABS
+    assert stamp() == (15 if reuse else 5)
+
+
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 7, 8, 32])
+@pytest.mark.parametrize("batch", [1, 5, 9])
+def test_split_k_vs_oracle_and_bitwise_v3(split, batch, cuda_device):
+    M, K = 300, 4096
+    packed, scales, x = make_problem(M, K, batch, seed=5 * split + batch)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    y4 = capi_gemv(tp, ts, tx, cfg(version=4, split_k=split))
+    assert stamp() == 4
+    y3 = capi_gemv(tp, ts, tx, cfg(version=3))
+    assert max_err(y4, ref) < MAX_ABS
+    assert torch.equal(y4, y3), "split-K must replay the canonical reduction order"
+
+
+@pytest.mark.parametrize("wpr", [1, 2, 3, 4, 8])
+def test_warps_per_row(wpr, cuda_device):
+    M, K = 256, 1024
+    packed, scales, x = make_problem(M, K, 3, seed=3)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = capi_gemv(tp, ts, tx, cfg(version=1, warps_per_row=wpr))
+    assert max_err(y, ref) < MAX_ABS
+    assert stamp() == (1 if wpr == 1 else 10 + wpr)
+
+
+def test_tensor_core_family_is_bitwise_identical(cuda_device):
+    M, K, B = 777, 11008, 5
+    packed, scales, x = make_problem(M, K, B, seed=11)
+    tp, ts, tx = to_device(packed, scales, x)
+    outs = [capi_gemv(tp, ts, tx, cfg(version=v, split_k=4)) for v in (2, 3, 4, 5)]
+    outs.append(capi_gemv(tp, ts, tx, cfg(version=5, reuse_weights=1)))
+    for y in outs[1:]:
+        assert torch.equal(y, outs[0])
+
+
+def test_batch_rows_are_independent(cuda_device):
+    # y[b] must not depend on which other rows share the call (bitwise).
+    M, K, B = 512, 4096, 33
+    packed, scales, x = make_problem(M, K, B, seed=21)
+    tp, ts, tx = to_device(packed, scales, x)
+    full = capi_gemv(tp, ts, tx, cfg())
+    for b in (0, 7, 8, 31, 32):
+        one = capi_gemv(tp, ts, tx[b:b + 1].contiguous(), cfg())
+        assert torch.equal(one[0], full[b])
+
+
+def test_row_slices_are_independent(cuda_device):
+    # A row shard of W gives exactly the matching slice of y (the property the
+    # row-parallel multi-GPU path relies on).
+    M, K, B = 4096, 4096, 2
+    packed, scales, x = make_problem(M, K, B, seed=22)
+    tp, ts, tx = to_device(packed, scales, x)
+    full = capi_gemv(tp, ts, tx, cfg())
+    for a, b in ((0, 512), (512, 1024), (1000, 1377), (4095, 4096)):
+        part = capi_gemv(tp[a:b].contiguous(), ts[a:b].contiguous(), tx, cfg())
+        assert torch.equal(part, full[:, a:b])
+
+
+def test_minus_eight_nibbles(cuda_device):
+    # The quantizer never emits -8, but the format decodes it.
+    M, K = 32, 256
+    packed = np.full((M, K // 8), np.int32(-0x77777778), np.int32)  # 0x88888888
+    scales = np.full((M, K // 128), np.float16(0.5)).view(np.uint16)
+    x = np.random.default_rng(0).standard_normal((2, K)).astype(np.float16)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    for v in range(6):
+        assert max_err(capi_gemv(tp, ts, tx, cfg(version=v)), ref) < MAX_ABS
+
+
+def test_k_zero_writes_zeros(cuda_device):
+    from decode_kernel import capi
+
+    y = torch.full((3, 64), 7.0, dtype=torch.float16, device="cuda")
+    st = capi.gemv(16, 16, 16, y.data_ptr(), 64, 0, 3, cfg())
+    assert st == capi.DK_OK
+    torch.cuda.synchronize()
+    assert (y == 0).all()
+
+
+def test_workspace_too_small_is_reported(cuda_device):
+    from decode_kernel import capi
+
+    packed, scales, x = make_problem(64, 1024, 1, seed=1)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = torch.empty((1, 64), dtype=torch.float16, device="cuda")
+    c = cfg(version=4, split_k=4)
+    need = capi.workspace_bytes(64, 1024, 1, c)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    st = capi.gemv(tp.data_ptr(), ts.data_ptr(), tx.data_ptr(), y.data_ptr(), 64, 1024, 1, c,
+                   ws.data_ptr(), need - 4, 0)
+    assert st == capi.DK_ERR_WORKSPACE
+
+
+def test_pdl_chain_matches_plain(cuda_device):
+    # Back-to-back launches with programmatic dependent launch: each GEMV's
+    # output feeds the next GEMV's x, so the dependency wait must hold.
+    from decode_kernel import capi
+
+    K = 1024
+    layers = [make_problem(K, K, 1, seed=40 + i, std=0.03) for i in range(6)]
+    dev = [to_device(p, s, x) for p, s, x in layers]
+    x0 = dev[0][2]
+    outs = {}
+    for flags in (0, capi.DK_FLAG_PDL):
+        h = x0
+        for tp, ts, _ in dev:
+            h = capi_gemv(tp, ts, h, cfg(flags=flags), poison=False)
+        torch.cuda.synchronize()
+        outs[flags] = h
+    assert torch.equal(outs[0], outs[capi.DK_FLAG_PDL])
+    assert capi.load().dk_device_error(-1, 1) == 0
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (4096, 11008)])
+@pytest.mark.parametrize("batch", [1, 8])
+def test_baseline_shapes(shape, batch, cuda_device):
+    M, K = shape
+    packed, scales, x = make_problem(M, K, batch, seed=2024)
+    ref = oracle_y(x, packed, scales)
+    tp, ts, tx = to_device(packed, scales, x)
+    for c in (cfg(), cfg(reuse_weights=1), cfg(version=2), cfg(version=4, split_k=4)):
+        assert max_err(capi_gemv(tp, ts, tx, c), ref) < MAX_ABS
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("shape", [(28672, 8192), (8192, 28672), (8192, 8192)])
+@pytest.mark.parametrize("batch", [1, 8])
+def test_llama70b_shapes_sampled_rows(shape, batch, cuda_device):
+    M, K = shape
+    packed, scales, x = make_problem(M, K, batch, seed=70)
+    rng = np.random.default_rng(1)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = capi_gemv(tp, ts, tx, cfg())
+    for a in rng.integers(0, M - 64, size=4):
+        rows = (int(a), int(a) + 64)
+        ref = oracle_y(x, packed, scales, rows=rows)
+        assert max_err(y, ref, rows=rows) < MAX_ABS
+    yr = capi_gemv(tp, ts, tx, cfg(reuse_weights=1))
+    assert torch.equal(yr, y)
