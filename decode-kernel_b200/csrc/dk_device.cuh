@@ -3,8 +3,9 @@
 // Everything here is sm_100a device code written directly in PTX where the
 // instruction matters: the LOP3 nibble-to-fp16 unpack, the m16n8k16 HMMA used
 // as an fp32-accumulating dot-product unit, mbarrier waits with an iteration
-// and wall-clock bound, 1-D bulk async copies (cp.async.bulk, the TMA engine's
-// untiled form) and the programmatic-dependent-launch controls.
+// and wall-clock bound, TMA copies (tensor-map boxes and 1-D bulk copies),
+// cp.async completion on mbarriers and the programmatic-dependent-launch
+// controls.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -187,6 +188,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to `ns`) instead of spinning through issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -203,10 +218,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                                                   volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
     if (*abort_flag) return false;
-    if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
       atomicExch(&g_dk_device_error, kDevWaitTimeout);
       *abort_flag = 1;
       return false;
@@ -225,6 +240,55 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst_smem),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Tensor-map TMA load of a 3-D box into this CTA's shared memory, completing
+// the box's bytes of transaction count on `bar`.  c0 is the innermost
+// coordinate (bytes inside a 128-byte strip; always 0 here, so 16-byte
+// aligned).  Box parts outside the tensor are zero-filled.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const void* tmap, int c0, int c1,
+                                            int c2, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, const uint32_t (&v)[4]) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
+__device__ __forceinline__ float lds_half(uint32_t addr) {
+  unsigned short h;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
+  return __half2float(__ushort_as_half(h));
+}
+
+// 4-byte Ampere-style async copy global -> shared (through L1).
+__device__ __forceinline__ void cp_async4(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+
+// Arrives on `bar` once every cp.async this thread issued so far has landed;
+// counts toward the barrier's expected arrivals (no pending-count increment).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// L2 policy for data every CTA re-reads (the activations).
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 // L2 policy for data read exactly once per call (the packed weights).

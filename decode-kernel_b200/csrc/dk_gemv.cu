@@ -20,9 +20,10 @@
 //                       workspace and the last CTA of a tile sums them in
 //                       split order (deterministic, one launch).
 //   v5  k_stream        persistent CTAs, one per SM: a producer warp streams
-//                       the CTA's contiguous row block into a 6-stage shared
-//                       memory ring with 1-D bulk async copies (TMA engine,
-//                       mbarrier transaction counts); 8 consumer warps unpack
+//                       the CTA's row block through a shared-memory ring, one
+//                       tensor-map TMA box (16 rows x 2 KB, 128-byte swizzle)
+//                       per stage plus the stage's scales by cp.async, all
+//                       completing on one mbarrier; 16 consumer warps unpack
 //                       and feed HMMA.  The default and fastest path.
 //   15  k_stream<reuse> the batch weight-reuse path: the same pipeline; every
 //                       weight byte is read from HBM once and applied to up to
@@ -37,6 +38,11 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #define DK_DEVICE_GLOBALS
 #include "dk_device.cuh"
@@ -52,6 +58,8 @@ struct GemvParams {
   int M, K, B;
   float* ws;               // v4: [K/128][B][M] fp32 per-group products
   unsigned* counters;      // v4: one arrival counter per 16-row tile
+  int stages;              // v5: ring depth
+  int xs_bytes;            // v5: bytes of x staged in shared memory (0 = none)
 };
 
 // ---------------------------------------------------------------------------
@@ -74,41 +82,58 @@ __device__ __forceinline__ float dot8_f32(const uint32_t (&h)[4], const uint4& x
 }
 
 // x fragment loads for one group: thread (g, c) of a warp needs
-// x[nt*8 + g][kx + 8t .. kx + 8t + 7], t = 0..3, kx = 128*G + 32*c.
+// x[nt*8 + g][kx + 8t .. kx + 8t + 7], t = 0..3, kx = 128*G + 32*c.  Lanes
+// whose batch column is past B read row B-1 instead: mma columns are
+// independent and those columns are never stored.
 template <int NT>
 __device__ __forceinline__ void load_x_group(const __half* __restrict__ x, int K, int B, int kx,
                                              int g, uint4 (&xr)[NT][4]) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int b = nt * 8 + g;
+    const __half* xb = x + (size_t)min(nt * 8 + g, B - 1) * K + kx;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      xr[nt][t] = (b < B) ? ldg_keep(x + (size_t)b * K + kx + 8 * t) : make_uint4(0, 0, 0, 0);
-    }
+    for (int t = 0; t < 4; ++t) xr[nt][t] = ldg_keep(xb + 8 * t);
   }
 }
 
 // One group (128 k) of a 16-row tile: thread (g, c) holds words 4c..4c+3 of
 // the group for rows g (wa) and g+8 (wb).  Eight HMMAs; the quad's four
 // threads supply the 16 k of each one, all inside this group, so the group
-// scale can be applied to the fp32 result afterwards.
+// scale can be applied to the fp32 result afterwards.  The eight form two
+// independent accumulation chains (words 0-1 and words 2-3) that are added at
+// the end: D_G = chain01 + chain23.  Every kernel computes D_G this way.
+__device__ __forceinline__ void word_mma(float (&d)[4], uint32_t wa, uint32_t wb,
+                                         const uint32_t (&px)[4]) {
+  uint32_t ha[4], hb[4];
+  unpack_q8(wa, ha);
+  unpack_q8(wb, hb);
+  mma16816(d, ha[0], hb[0], ha[1], hb[1], px[0], px[1]);
+  mma16816(d, ha[2], hb[2], ha[3], hb[3], px[2], px[3]);
+}
+
+__device__ __forceinline__ void join_chains(float (&d)[4], const float (&e)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = __fadd_rn(d[i], e[i]);
+}
+
 template <int NT>
 __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb,
                                           const uint4 (&xr)[NT][4], float (&d)[NT][4]) {
   const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t Bw[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    uint32_t ha[4], hb[4];
-    unpack_q8(A[t], ha);
-    unpack_q8(Bw[t], hb);
+  for (int nt = 0; nt < NT; ++nt) {
+    float e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int t = 0; t < 4; ++t) {
       uint32_t px[4];
       pair_x8(xr[nt][t], px);
-      mma16816(d[nt], ha[0], hb[0], ha[1], hb[1], px[0], px[1]);
-      mma16816(d[nt], ha[2], hb[2], ha[3], hb[3], px[2], px[3]);
+      if (t < 2)
+        word_mma(d[nt], A[t], Bw[t], px);
+      else
+        word_mma(e, A[t], Bw[t], px);
     }
+    join_chains(d[nt], e);
   }
 }
 
@@ -116,9 +141,11 @@ __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb,
 // that all of them return the same bits for the same inputs (and y[b] does
 // not depend on which other batch rows or output rows are in the call):
 //   a_G      = fp32(scale[m, G] * D_G)   (D_G: the group's HMMA dot product)
-//   acc_w    = (((0 + a_w) + a_{w+8}) + a_{w+16}) + ...     for w = 0..7
-//   y        = fp16_rn((((0 + acc_0) + acc_1) + ...) + acc_7)
+//   acc_w    = (((0 + a_w) + a_{w+16}) + a_{w+32}) + ...   for w = 0..15
+//   y        = fp16_rn((((0 + acc_0) + acc_1) + ...) + acc_15)
 // Explicit _rn intrinsics keep the compiler from contracting mul+add.
+constexpr int kClasses = 16;
+
 template <int NT>
 __device__ __forceinline__ void scale_accumulate(float (&acc)[NT][4], const float (&d)[NT][4],
                                                  float sa, float sb) {
@@ -290,9 +317,9 @@ __device__ __forceinline__ void split_k_finish(const GemvParams& p, int rows, in
     const float* a = p.ws + (size_t)b * p.M + trow + r;
     const size_t gstride = (size_t)p.B * p.M;
     float y = 0.f;
-    for (int w = 0; w < kTileWarps; ++w) {
+    for (int w = 0; w < kClasses; ++w) {
       float acc = 0.f;
-      for (int G = w; G < groups; G += kTileWarps) acc = __fadd_rn(acc, __ldcg(a + G * gstride));
+      for (int G = w; G < groups; G += kClasses) acc = __fadd_rn(acc, __ldcg(a + G * gstride));
       y = __fadd_rn(y, acc);
     }
     p.y[(size_t)b * p.M + trow + r] = __float2half_rn(y);
@@ -321,7 +348,7 @@ template <int NT, int MODE>
 __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
   write_stamp(MODE == kTileDirect ? 2 : MODE == kTileScales ? 3 : 4);
   constexpr int W = 8 * NT;
-  __shared__ float red[kTileWarps][16 * W];
+  __shared__ float red[kClasses][16 * W];
   extern __shared__ __half s_scales[];  // kTileScales: [16][groups in range]
   __shared__ unsigned s_last;
 
@@ -365,9 +392,15 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
     __syncthreads();
   }
 
-  float acc[NT][4];
+  // Warp w covers groups G = w (mod 8), i.e. classes w and w + 8 of the
+  // canonical order; acc[j] holds the class reached on the j-th parity step.
+  float acc[2][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      acc[j][nt][0] = acc[j][nt][1] = acc[j][nt][2] = acc[j][nt][3] = 0.f;
+  const int cls0 = ((g0 + warp) >> 3) & 1;  // class bit of this warp's first group
 
   for (int base = g0 + warp; base < g1; base += kTilePrefetch * kTileWarps) {
 #pragma unroll
@@ -398,7 +431,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
         if (MODE == kTileSplitK && gridDim.y > 1)
           store_group_products<NT>(p, d, sa, sb, G, trow, rows, g, c);
         else
-          scale_accumulate<NT>(acc, d, sa, sb);
+          scale_accumulate<NT>(acc[i & 1], d, sa, sb);
       }
     }
   }
@@ -407,54 +440,224 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
     split_k_finish(p, rows, trow, &s_last);
     return;
   }
-  store_fragment<NT>(red[warp], acc, g, c);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) store_fragment<NT>(red[warp + 8 * ((cls0 + j) & 1)], acc[j], g, c);
   __syncthreads();
   for (int o = threadIdx.x; o < 16 * W; o += blockDim.x) {
     const int r = o / W, b = o % W;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kTileWarps; ++w) s = __fadd_rn(s, red[w][o]);
+    for (int w = 0; w < kClasses; ++w) s = __fadd_rn(s, red[w][o]);
     if (r < rows && b < p.B) p.y[(size_t)b * p.M + trow + r] = __float2half_rn(s);
   }
 }
 
 
 // ---------------------------------------------------------------------------
-// v5: persistent bulk-copy pipeline.
+// v5: persistent TMA pipeline.
 //
-// CTA i owns rows [i*M/P, (i+1)*M/P): one contiguous span of packed bytes.
-// It walks that span as stages of (16-row tile) x (2048-k chunk).  A stage is
-// up to 16 row pieces of 1 KB, each one cp.async.bulk issued by its own lane
-// of the producer warp into a padded slot (row stride 1088 B, so rows g and
-// g+1 fall on opposite halves of the 32 banks and the consumers' 128-bit
-// shared loads are conflict-free).  6 slots keep ~100 KB in flight per SM,
-// which covers HBM latency x bandwidth / 148 SMs with room to spare.
+// CTA i owns rows [i*M/P, (i+1)*M/P).  It walks them as stages of (16-row
+// tile) x (4096-k chunk): 16 rows x 2 KB of packed weights.  When K is a
+// multiple of 256 the producer fetches a stage with ONE tensor-map TMA copy
+// (a 3-D view of the weights: 128-byte strips x rows x strips, 128-byte
+// swizzle) and the stage's 16 x 32 scales with 4-byte cp.async, all
+// completing on the stage's mbarrier; otherwise it issues one 1-D bulk copy
+// per row into rows padded to 2112 bytes and the consumers read the scales
+// from global memory one stage ahead.  Few, large copy operations matter on
+// B200: with ~100 KB in flight per SM, 1 KB copies stream at ~2.2 TB/s while
+// 16-32 KB tensor boxes reach ~5 TB/s.
+//
+// Bank conflicts: under the 128-byte swizzle, 16-byte chunk j of tile row r
+// sits at chunk position j ^ (r & 7).  A quarter-warp of the consumers' 128-bit
+// fragment loads covers two mma rows; mapping mma row g to tile row
+// {0,4,1,5,2,6,3,7}[g] (and g+8 to 8 + that) puts those two rows on opposite
+// halves of the banks, so every fragment load is conflict-free.  (The padded
+// bulk layout is conflict-free with the identity mapping.)
+//
+// Activations: when the pass's x rows fit in kXsMaxBytes the producer copies
+// them once into shared memory (after the PDL wait -- x may be the previous
+// kernel's output; each batch row padded by 64 bytes) and the consumers
+// rearrange every 128-k group so that a group's B fragments are four
+// conflict-free 128-bit loads: the pairs of word t for quad lane c sit at
+// 16 * (4t + c).  Larger x is read from global memory per group.  Batch lanes
+// past B read batch row B-1 (their columns are discarded).
+//
+// Tile results: every consumer warp stores its partial sums; one warp per tile
+// (rotating) adds the 16 classes in order and writes y while the others move
+// on -- two buffers guarded by mbarriers, no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
 namespace v5 {
-constexpr int kChunkK = 2048;
-constexpr int kChunkGroups = kChunkK / kGroup;  // 16
-constexpr int kRowBytes = kChunkK / 2;          // 1024
-constexpr int kRowStride = kRowBytes + 64;      // 1088
-constexpr int kStageBytes = 16 * kRowStride;    // 17408
-constexpr int kStages = 6;
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-}  // namespace v5
+constexpr int kChunkK = 4096;                   // k per stage
+constexpr int kChunkGroups = kChunkK / kGroup;  // 32
+constexpr int kRowBytes = kChunkK / 2;          // 2048 bytes of a row per stage
+constexpr int kPadRowStride = kRowBytes + 64;   // 2112 (bulk path)
+constexpr int kStageBytesBulk = 16 * kPadRowStride;    // 33792
+constexpr int kStageBytesTma = 16 * kRowBytes;         // 32768
+constexpr int kScaleRowStride = kChunkGroups * 2 + 4;  // 68: rows land on distinct banks
+constexpr int kStageScaleBytes = 16 * kScaleRowStride;  // 1088 (TMA path)
+constexpr int kStrip = 128;                             // bytes per swizzle strip
+constexpr int kStripsPerChunk = kRowBytes / kStrip;     // 16
+constexpr int kMaxStages = 6;
+constexpr int kMinStages = 2;
+// Warp w handles groups w and w + 16 of every stage: class w of the canonical
+// order (G mod 16 == w), in ascending G.
+constexpr int kConsumerWarps = 16;
+constexpr int kGroupsPerWarp = kChunkGroups / kConsumerWarps;  // 2
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;  // + 1 producer warp
+constexpr int kXsMaxBytes = 68 * 1024;
+constexpr int kXsMaxChunksPerThread =
+    (kXsMaxBytes / 16 + kConsumerThreads - 1) / kConsumerThreads;
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int kSmemCap = 227 * 1024;  // per-CTA opt-in maximum on sm_100
 
-template <int NT>
-struct StreamSmem {
-  alignas(128) uint8_t stage[v5::kStages][v5::kStageBytes];
-  float red[2][v5::kConsumerWarps][16 * 8 * NT];
-  uint64_t full[v5::kStages];
-  uint64_t empty[v5::kStages];
-  int abort_flag;
+__host__ __device__ constexpr int stage_bytes(bool tmap) {
+  return tmap ? kStageBytesTma : kStageBytesBulk;
+}
+__host__ __device__ inline int xs_row_stride(int K) { return 2 * K + 64; }
+
+struct Layout {
+  int sc_off, xs_off, red_off, bar_off, total;
 };
 
-template <int NT, int STAMP>
-__global__ void __launch_bounds__(v5::kThreads, 1) k_stream(GemvParams p) {
+__host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_bytes) {
+  Layout L;
+  int off = stages * stage_bytes(tmap);
+  L.sc_off = off;
+  off += tmap ? (stages * kStageScaleBytes + 127) / 128 * 128 : 0;
+  L.xs_off = off;
+  off += (xs_bytes + 127) / 128 * 128;
+  L.red_off = off;
+  off += 2 * kConsumerWarps * 16 * 8 * nt * (int)sizeof(float);
+  L.bar_off = off;
+  off += (2 * kMaxStages + 5) * 8 + 16;  // full, empty, x, red_full[2], red_free[2], flag
+  L.total = off;
+  return L;
+}
+}  // namespace v5
+
+// Stage walker: (tile, chunk) in tile-major order plus the ring slot/round,
+// advanced without divisions.
+struct StageCursor {
+  int tile = 0, chunk = 0, slot = 0, round = 0;
+  __device__ __forceinline__ void next(int nk, int stages) {
+    if (++chunk == nk) {
+      chunk = 0;
+      ++tile;
+    }
+    if (++slot == stages) {
+      slot = 0;
+      ++round;
+    }
+  }
+};
+
+// Tile row that mma row r (0..15) reads.
+template <bool TMAP>
+__device__ __forceinline__ int tile_row(int r) {
+  if constexpr (TMAP) return (r & 8) | ((r & 1) << 2) | ((r >> 1) & 3);
+  return r;
+}
+
+// Offset inside a stage of quad lane c's 16 bytes of group gi in tile row R.
+template <bool TMAP>
+__device__ __forceinline__ uint32_t frag_off(int R, int gi, int c) {
+  if constexpr (TMAP) {
+    const int j = ((gi & 1) << 2) | c;  // 16-byte chunk inside the 128-byte strip
+    return (gi >> 1) * (16 * v5::kStrip) + R * v5::kStrip + ((j ^ (R & 7)) << 4);
+  }
+  return R * v5::kPadRowStride + gi * 64 + c * 16;
+}
+
+// One group, B fragments from the rearranged shared copy of x (two chains,
+// same arithmetic as group_mma).
+__device__ __forceinline__ void group_mma_xs(const uint4& wa, const uint4& wb, uint32_t xq,
+                                             float (&d)[4]) {
+  const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t Bw[4] = {wb.x, wb.y, wb.z, wb.w};
+  float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint4 x4 = lds128(xq + 64 * t);
+    const uint32_t px[4] = {x4.x, x4.y, x4.z, x4.w};
+    if (t < 2)
+      word_mma(d, A[t], Bw[t], px);
+    else
+      word_mma(e, A[t], Bw[t], px);
+  }
+  join_chains(d, e);
+}
+
+// One group with x read from global memory, for the streaming kernel: the
+// weights are unpacked once and reused for every n-tile, and x is loaded one
+// n-tile at a time (register budget at 544 threads).  Same HMMA chains as
+// group_mma, so the same bits.
+template <int NT>
+__device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
+                                             const __half* __restrict__ x, int K, int B, int kx,
+                                             int g, float (&d)[NT][4]) {
+  const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t Bw[4] = {wb.x, wb.y, wb.z, wb.w};
+  uint32_t ha[4][4], hb[4][4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    unpack_q8(A[t], ha[t]);
+    unpack_q8(Bw[t], hb[t]);
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const __half* xb = x + (size_t)min(nt * 8 + g, B - 1) * K + kx;
+    uint4 xr[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) xr[t] = ldg_keep(xb + 8 * t);
+    float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t px[4];
+      pair_x8(xr[t], px);
+      float(&acc)[4] = (t < 2) ? d[nt] : e;
+      mma16816(acc, ha[t][0], hb[t][0], ha[t][1], hb[t][1], px[0], px[1]);
+      mma16816(acc, ha[t][2], hb[t][2], ha[t][3], hb[t][3], px[2], px[3]);
+    }
+    join_chains(d[nt], e);
+  }
+}
+
+// Producer helper: copy this pass's x rows into padded shared rows.
+__device__ __forceinline__ void fetch_x(const GemvParams& p, uint32_t xs, uint64_t* xbar,
+                                        int lane) {
+  const uint32_t row_bytes = 2u * (uint32_t)p.K;
+  const uint32_t pieces = (row_bytes + 4095u) / 4096u;
+  if (lane == 0) mbar_arrive_expect_tx(xbar, row_bytes * (uint32_t)p.B);
+  __syncwarp();
+  const uint64_t keep = policy_evict_last();
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x);
+  for (uint32_t i = lane; i < pieces * (uint32_t)p.B; i += 32) {
+    const uint32_t b = i / pieces, o = (i % pieces) * 4096u;
+    bulk_g2s(xs + b * (uint32_t)v5::xs_row_stride(p.K) + o, src + (size_t)b * row_bytes + o,
+             min(4096u, row_bytes - o), xbar, keep);
+  }
+}
+
+template <int NT, int STAMP, bool XS, bool TMAP>
+__global__ void __launch_bounds__(v5::kThreads, 1)
+    k_stream(const __grid_constant__ CUtensorMap tmap, GemvParams p) {
   using namespace v5;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  StreamSmem<NT>& sm = *reinterpret_cast<StreamSmem<NT>*>(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int kStageBytes = stage_bytes(TMAP);
+  constexpr int W = 8 * NT;  // output columns per tile row in the reduction buffer
+  const int stages = p.stages;
+  const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* xbar = empty + kMaxStages;
+  uint64_t* red_full = xbar + 1;      // [2]: all consumer warps stored a tile
+  uint64_t* red_free = red_full + 2;  // [2]: the tile's reducer has read it
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + 2);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t scs = smem_u32(smem + L.sc_off);
+  const uint32_t xs = smem_u32(smem + L.xs_off);
   write_stamp(STAMP);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -466,47 +669,88 @@ __global__ void __launch_bounds__(v5::kThreads, 1) k_stream(GemvParams p) {
   const int total = ntiles * nk;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kConsumerWarps);
+    for (int s = 0; s < stages; ++s) {
+      // TMA path: the box's transaction bytes (1 arrival) plus one cp.async
+      // arrival per producer lane for the stage's scales.
+      mbar_init(&full[s], TMAP ? 33 : 1);
+      mbar_init(&empty[s], kConsumerWarps);
     }
-    sm.abort_flag = 0;
+    mbar_init(xbar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&red_full[i], kConsumerWarps);
+      mbar_init(&red_free[i], 1);
+    }
+    *abort_flag = 0;
     fence_barrier_init();
+    if constexpr (TMAP) tma_prefetch_desc(&tmap);
   }
   __syncthreads();
   // A dependent GEMV launched with PDL may now start streaming its weights.
   pdl_trigger();
-  volatile int* abort_flag = &sm.abort_flag;
 
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     const uint64_t policy = policy_evict_first();
     const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(p.packed);
     const size_t row_bytes = (size_t)p.K / 2;
+    const int prefill = min(stages, total);
+    StageCursor cur;
     int issued = 0;
     for (int s = 0; s < total; ++s) {
-      const int slot = s % kStages;
-      if (s >= kStages && !mbar_wait_bounded(&sm.empty[slot], ((s / kStages) - 1) & 1, abort_flag))
+      if (XS && s == prefill) {
+        // Weights for the first `prefill` stages are in flight; now wait for
+        // the predecessor grid and fetch x (it may be its output).
+        pdl_wait();
+        fetch_x(p, xs, xbar, lane);
+      }
+      if (s >= stages && !mbar_wait_bounded(&empty[cur.slot], (cur.round - 1) & 1, abort_flag))
         break;
-      const int tile = s / nk, chunk = s % nk;
-      const int trow = r0 + tile * 16;
-      const int rows = min(16, r1 - trow);
-      const uint32_t bytes = (uint32_t)min(kChunkGroups, groups - chunk * kChunkGroups) * 64u;
-      if (lane == 0) mbar_arrive_expect_tx(&sm.full[slot], bytes * (uint32_t)rows);
-      __syncwarp();
-      if (lane < rows) {
-        bulk_g2s(smem_u32(sm.stage[slot]) + lane * kRowStride,
-                 wbytes + (size_t)(trow + lane) * row_bytes + (size_t)chunk * kRowBytes, bytes,
-                 &sm.full[slot], policy);
+      const int trow = r0 + cur.tile * 16;
+      const uint32_t dst = ring + cur.slot * kStageBytes;
+      if constexpr (TMAP) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
+          tma_load_3d(dst, &tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot], policy);
+        }
+        // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups) per
+        // cp.async.  K % 256 == 0 here, so scale rows are 4-byte aligned.
+        const uint32_t sdst = scs + cur.slot * kStageScaleBytes;
+        const int gbase = cur.chunk * kChunkGroups;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
+          if (trow + r < p.M && gbase + w2 < groups)
+            cp_async4(sdst + r * kScaleRowStride + w2 * 2,
+                      p.scales + (size_t)(trow + r) * groups + gbase + w2);
+        }
+        cp_async_mbar_arrive(&full[cur.slot]);
+      } else {
+        const int rows = min(16, r1 - trow);
+        const uint32_t bytes =
+            (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
+        if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
+        __syncwarp();
+        if (lane < rows) {
+          bulk_g2s(dst + lane * kPadRowStride,
+                   wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
+                   bytes, &full[cur.slot], policy);
+        }
       }
       issued = s + 1;
+      cur.next(nk, stages);
+    }
+    if (XS && prefill == total && total > 0) {
+      // Every stage fit in the first fill: x has not been fetched yet.
+      pdl_wait();
+      fetch_x(p, xs, xbar, lane);
     }
     if (*abort_flag && lane == 0) {
       // Let copies already in flight land before the CTA's shared memory is
       // released (bounded as well, against a fresh clock).
       volatile int no_abort = 0;
-      for (int s = max(0, issued - kStages); s < issued; ++s)
-        mbar_wait_bounded(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);
+      for (int s = max(0, issued - stages); s < issued; ++s)
+        mbar_wait_bounded(&full[s % stages], (s / stages) & 1, &no_abort);
+      if (XS) mbar_wait_bounded(xbar, 0, &no_abort);
     }
     return;
   }
@@ -514,69 +758,146 @@ __global__ void __launch_bounds__(v5::kThreads, 1) k_stream(GemvParams p) {
   // ---------------- consumers ----------------
   pdl_wait();  // x and y belong to the predecessor until here
   const int g = lane >> 2, c = lane & 3;
+  const int ra = tile_row<TMAP>(g), rb = tile_row<TMAP>(g + 8);  // this lane's tile rows
+  const int bb = min(g, p.B - 1);  // batch row this lane feeds into the mma
+  const int xrow = xs_row_stride(p.K);
+  if (XS) {
+    // Rearrange each 128-k group of x: raw 16-byte chunk i holds k = 8i..8i+7,
+    // i.e. word t = i % 4 of quad lane c = i / 4; it moves, with its pairs
+    // (x0,x4),(x1,x5),(x2,x6),(x3,x7), to chunk 4t + c.  All chunks are read
+    // before any is written.
+    const bool ok = mbar_wait_bounded(xbar, 0, abort_flag);
+    const int nchunks = p.B * groups * 16;
+    uint4 v[kXsMaxChunksPerThread];
+    uint32_t dst[kXsMaxChunksPerThread];
+#pragma unroll
+    for (int u = 0; u < kXsMaxChunksPerThread; ++u) {
+      const int q = threadIdx.x + u * kConsumerThreads;
+      if (ok && q < nchunks) {
+        const int i = q & 15, blk = q >> 4;
+        const uint32_t base = xs + (blk / groups) * xrow + (blk % groups) * 256;
+        v[u] = lds128(base + 16 * i);
+        dst[u] = base + 16 * (4 * (i & 3) + (i >> 2));
+      }
+    }
+    named_barrier(1, kConsumerThreads);
+#pragma unroll
+    for (int u = 0; u < kXsMaxChunksPerThread; ++u) {
+      const int q = threadIdx.x + u * kConsumerThreads;
+      if (ok && q < nchunks) {
+        uint32_t pr[4];
+        pair_x8(v[u], pr);
+        sts128(dst[u], pr);
+      }
+    }
+    named_barrier(1, kConsumerThreads);
+  }
+
+  // Per-thread offsets, fixed for the whole kernel.
+  uint32_t offa[kGroupsPerWarp], offb[kGroupsPerWarp];
+#pragma unroll
+  for (int j = 0; j < kGroupsPerWarp; ++j) {
+    offa[j] = frag_off<TMAP>(ra, warp + j * kConsumerWarps, c);
+    offb[j] = frag_off<TMAP>(rb, warp + j * kConsumerWarps, c);
+  }
+  const uint32_t sc_a = ra * kScaleRowStride + warp * 2, sc_b = rb * kScaleRowStride + warp * 2;
+  const uint32_t xq = xs + bb * xrow + 16 * c;  // + 256 G + 64 t
+
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 
-  for (int s = 0; s < total; ++s) {
-    const int slot = s % kStages;
-    const int tile = s / nk, chunk = s % nk;
-    const int trow = r0 + tile * 16;
+  // Bulk path: scales from global memory, loaded one stage ahead.
+  float sn[kGroupsPerWarp][2];
+  auto load_scales = [&](const StageCursor& q) {
+    const int trow = r0 + q.tile * 16;
     const int rows = min(16, r1 - trow);
-    const int cg = min(kChunkGroups, groups - chunk * kChunkGroups);
-
-    // x for this warp's first group of the stage, before waiting on the data.
-    uint4 xr[NT][4];
-    if (warp < cg) load_x_group<NT>(p.x, p.K, p.B, (chunk * kChunkGroups + warp) * kGroup + 32 * c, g, xr);
-
-    if (mbar_wait_bounded(&sm.full[slot], (s / kStages) & 1, abort_flag)) {
-      const uint32_t st = smem_u32(sm.stage[slot]);
-      const __half* sa_ptr = p.scales + (size_t)(trow + min(g, rows - 1)) * groups;
-      const __half* sb_ptr = p.scales + (size_t)(trow + min(g + 8, rows - 1)) * groups;
-      for (int gi = warp; gi < cg; gi += kConsumerWarps) {
-        const int G = chunk * kChunkGroups + gi;
-        const uint4 wa = lds128(st + g * kRowStride + gi * 64 + c * 16);
-        const uint4 wb = lds128(st + (g + 8) * kRowStride + gi * 64 + c * 16);
-        const float sa = ldg_half(sa_ptr + G);
-        const float sb = ldg_half(sb_ptr + G);
-        float d[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-        if constexpr (NT == 1) {
-          // Double-buffer x: the next group's loads overlap this group's math.
-          uint4 xc[NT][4];
+    for (int j = 0; j < kGroupsPerWarp; ++j) {
+      const int G = min(q.chunk * kChunkGroups + warp + j * kConsumerWarps, groups - 1);
+      sn[j][0] = ldg_half(p.scales + (size_t)(trow + min(ra, rows - 1)) * groups + G);
+      sn[j][1] = ldg_half(p.scales + (size_t)(trow + min(rb, rows - 1)) * groups + G);
+    }
+  };
+  StageCursor cur;
+  if (!TMAP && total > 0) load_scales(cur);
+
+  for (int s = 0; s < total; ++s) {
+    const int trow = r0 + cur.tile * 16;
+    const int rows = min(16, r1 - trow);
+    const int cg = min(kChunkGroups, groups - cur.chunk * kChunkGroups);
+    float sc[kGroupsPerWarp][2];
+    if (!TMAP) {
 #pragma unroll
-          for (int t = 0; t < 4; ++t) xc[0][t] = xr[0][t];
-          if (gi + kConsumerWarps < cg)
-            load_x_group<NT>(p.x, p.K, p.B, (G + kConsumerWarps) * kGroup + 32 * c, g, xr);
-          group_mma<NT>(wa, wb, xc, d);
-        } else {
-          if (gi != warp) load_x_group<NT>(p.x, p.K, p.B, G * kGroup + 32 * c, g, xr);
-          group_mma<NT>(wa, wb, xr, d);
+      for (int j = 0; j < kGroupsPerWarp; ++j) sc[j][0] = sn[j][0], sc[j][1] = sn[j][1];
+    }
+    StageCursor nxt = cur;
+    nxt.next(nk, stages);
+    if (!TMAP && s + 1 < total) load_scales(nxt);
+
+    if (mbar_wait_bounded(&full[cur.slot], cur.round & 1, abort_flag)) {
+      const uint32_t st = ring + cur.slot * kStageBytes;
+      const uint32_t sst = scs + cur.slot * kStageScaleBytes;
+#pragma unroll
+      for (int j = 0; j < kGroupsPerWarp; ++j) {
+        const int gi = warp + j * kConsumerWarps;
+        if (gi < cg) {
+          const int G = cur.chunk * kChunkGroups + gi;
+          const uint4 wa = lds128(st + offa[j]);
+          const uint4 wb = lds128(st + offb[j]);
+          if constexpr (TMAP) {
+            sc[j][0] = lds_half(sst + sc_a + j * 2 * kConsumerWarps);
+            sc[j][1] = lds_half(sst + sc_b + j * 2 * kConsumerWarps);
+          }
+          float d[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+          if constexpr (XS)
+            group_mma_xs(wa, wb, xq + 256u * G, d[0]);
+          else
+            group_mma_gx<NT>(wa, wb, p.x, p.K, p.B, G * kGroup + 32 * c, g, d);
+          scale_accumulate<NT>(acc, d, sc[j][0], sc[j][1]);
         }
-        scale_accumulate<NT>(acc, d, sa, sb);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    if (lane == 0) mbar_arrive(&empty[cur.slot]);
 
-    if (chunk == nk - 1) {
-      // Tile complete: sum the consumer warps' partials in warp order.
-      float* red = sm.red[tile & 1][0];
-      store_fragment<NT>(sm.red[tile & 1][warp], acc, g, c);
-      named_barrier(1, kConsumerWarps * 32);
-      constexpr int W = 8 * NT;
-      for (int o = threadIdx.x; o < 16 * W; o += kConsumerWarps * 32) {
-        const int r = o / W, b = o % W;
-        float sum = 0.f;
+    if (cur.chunk == nk - 1) {
+      // Tile complete.  Each warp stores its partials (class = warp); warp
+      // (tile % 16) sums the 16 classes in order and writes y, while the
+      // others move on.  Two buffers; a buffer is rewritten only after the
+      // reducer two tiles back has released it.
+      const int t = cur.tile, rs = t & 1;
+      float* rt = red + rs * kConsumerWarps * 16 * W;
+      if (t >= 2) mbar_wait_bounded(&red_free[rs], ((t >> 1) - 1) & 1, abort_flag);
+      float* mine = rt + warp * 16 * W;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) sum = __fadd_rn(sum, red[w * 16 * W + o]);
-        if (r < rows && b < p.B && !*abort_flag)
-          p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
+      for (int nt = 0; nt < NT; ++nt) {
+        mine[ra * W + nt * 8 + 2 * c] = acc[nt][0];
+        mine[ra * W + nt * 8 + 2 * c + 1] = acc[nt][1];
+        mine[rb * W + nt * 8 + 2 * c] = acc[nt][2];
+        mine[rb * W + nt * 8 + 2 * c + 1] = acc[nt][3];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[rs]);
+      if (warp == (t & (kConsumerWarps - 1))) {
+        if (mbar_wait_bounded(&red_full[rs], (t >> 1) & 1, abort_flag)) {
+          for (int o = lane; o < 16 * W; o += 32) {
+            const int r = o / W, b = o % W;
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) sum = __fadd_rn(sum, rt[w * 16 * W + o]);
+            if (r < rows && b < p.B) p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_free[rs]);
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     }
+    cur = nxt;
   }
 }
 
@@ -587,9 +908,9 @@ __global__ void __launch_bounds__(v5::kThreads, 1) k_stream(GemvParams p) {
 constexpr int kStampReuse = 15;
 constexpr int kMaxBatchPerPass = 32;  // 4 mma n-tiles
 
-template <typename Kern>
-dk_status launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                 bool pdl, const GemvParams& p, const char* name) {
+template <typename Kern, typename... Args>
+dk_status launch(const char* name, Kern kernel, dim3 grid, dim3 block, size_t smem,
+                 cudaStream_t stream, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -602,7 +923,7 @@ dk_status launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
   if (e != cudaSuccess) {
     set_cuda_error(e, name);
     return DK_ERR_LAUNCH;
@@ -616,8 +937,13 @@ dk_status ensure_smem(Kern kernel, size_t bytes, std::atomic<unsigned long long>
   const int dev = current_device();
   const unsigned long long bit = 1ull << (dev & 63);
   if (done.load(std::memory_order_acquire) & bit) return DK_OK;
-  const cudaError_t e =
+  cudaError_t e =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  // Without this the driver may size the SM's shared-memory carveout for one
+  // small CTA and leave no room for a second resident CTA.
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) {
     set_cuda_error(e, "cudaFuncSetAttribute");
     return DK_ERR_CUDA;
@@ -626,15 +952,97 @@ dk_status ensure_smem(Kern kernel, size_t bytes, std::atomic<unsigned long long>
   return DK_OK;
 }
 
-template <int NT, int STAMP>
-dk_status launch_stream(const GemvParams& p, cudaStream_t st, bool pdl) {
+// Tensor map of the packed weights for the v5 TMA path: a 3-D view
+// {128-byte strip, row, strip index} with strides {K/2, 128} bytes, boxes of
+// 16 rows x 16 strips (32 KB), 128-byte swizzle.  Encoded once per
+// (pointer, M, K) -- the map holds nothing else -- and kept in a small cache.
+using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
+  struct Entry {
+    const void* ptr;
+    int M, K;
+    unsigned long long stamp;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static unsigned long long clock = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  Entry* victim = &cache[0];
+  for (Entry& e : cache) {
+    if (e.stamp && e.ptr == packed && e.M == M && e.K == K) {
+      e.stamp = ++clock;
+      *out = e.map;
+      return true;
+    }
+    if (e.stamp < victim->stamp) victim = &e;
+  }
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)v5::kStrip, (cuuint64_t)M, (cuuint64_t)(K / 256)};
+  cuuint64_t strides[2] = {(cuuint64_t)K / 2, (cuuint64_t)v5::kStrip};
+  cuuint32_t box[3] = {(cuuint32_t)v5::kStrip, 16u, (cuuint32_t)v5::kStripsPerChunk};
+  cuuint32_t elem[3] = {1, 1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(packed), dims, strides, box,
+          elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  victim->ptr = packed;
+  victim->M = M;
+  victim->K = K;
+  victim->stamp = ++clock;
+  victim->map = map;
+  *out = map;
+  return true;
+}
+
+template <int NT, int STAMP, bool XS, bool TMAP>
+dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t st, bool pdl) {
   static std::atomic<unsigned long long> smem_done{0};
-  const size_t smem = sizeof(StreamSmem<NT>);
-  dk_status s = ensure_smem(k_stream<NT, STAMP>, smem, smem_done);
+  p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
+  p.stages = v5::kMaxStages;
+  while (p.stages > v5::kMinStages &&
+         v5::layout(NT, TMAP, p.stages, p.xs_bytes).total > v5::kSmemBudget)
+    --p.stages;
+  const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes).total;
+  if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
+  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
   const int grid = std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
-  return launch(k_stream<NT, STAMP>, dim3(grid), dim3(v5::kThreads), smem, st, pdl, p,
-                "k_stream");
+  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP>, dim3(grid), dim3(v5::kThreads), smem,
+                st, pdl, tmap, p);
+}
+
+template <int NT, int STAMP, bool TMAP>
+dk_status launch_stream_x(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
+                          bool pdl) {
+  if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
+    return launch_stream_cfg<1, STAMP, true, TMAP>(p, tmap, st, pdl);
+  return launch_stream_cfg<NT, STAMP, false, TMAP>(p, tmap, st, pdl);
+}
+
+template <int NT, int STAMP>
+dk_status launch_stream(const GemvParams& p, cudaStream_t st, bool pdl) {
+  CUtensorMap tmap;
+  if (p.K % 256 == 0 && weight_tensor_map(p.packed, p.M, p.K, &tmap))
+    return launch_stream_x<NT, STAMP, true>(p, tmap, st, pdl);
+  std::memset(&tmap, 0, sizeof(tmap));
+  return launch_stream_x<NT, STAMP, false>(p, tmap, st, pdl);
 }
 
 template <int NT, int MODE>
@@ -650,8 +1058,8 @@ dk_status launch_tile(const GemvParams& p, int split, cudaStream_t st, bool pdl)
       if (s != DK_OK) return s;
     }
   }
-  return launch(k_tile<NT, MODE>, dim3(tiles, MODE == kTileSplitK ? split : 1),
-                dim3(kTileWarps * 32), smem, st, pdl, p, "k_tile");
+  return launch("k_tile", k_tile<NT, MODE>, dim3(tiles, MODE == kTileSplitK ? split : 1),
+                dim3(kTileWarps * 32), smem, st, pdl, p);
 }
 
 template <int MODE>
@@ -785,15 +1193,15 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
     } else {
       switch (c.version) {
         case 0:
-          s = launch(k_row_scalar, dim3((M + 255) / 256), dim3(256), 0, st, pdl, p,
-                     "k_row_scalar");
+          s = launch("k_row_scalar", k_row_scalar, dim3((M + 255) / 256), dim3(256), 0, st, pdl,
+                     p);
           break;
         case 1:
           if (c.warps_per_row > 1) {
             const int wpr = std::max(2, std::min(c.warps_per_row, 8));
-            s = launch(k_block_row, dim3(M), dim3(wpr * 32), 0, st, pdl, p, "k_block_row");
+            s = launch("k_block_row", k_block_row, dim3(M), dim3(wpr * 32), 0, st, pdl, p);
           } else {
-            s = launch(k_warp_row, dim3((M + 3) / 4), dim3(128), 0, st, pdl, p, "k_warp_row");
+            s = launch("k_warp_row", k_warp_row, dim3((M + 3) / 4), dim3(128), 0, st, pdl, p);
           }
           break;
         case 2:
