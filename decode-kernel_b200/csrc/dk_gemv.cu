@@ -1223,6 +1223,67 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
   return DK_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Split-K without caller-provided memory.
+//
+// For callers that cannot allocate device memory at the point of the call --
+// code running inside an allocator hook, a graph-capture region or a host
+// runtime that owns every allocation itself -- the split-K path can use a
+// fixed scratch buffer that lives in this library's own device image instead
+// of a caller workspace.  Each device that loads the library holds it until
+// the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_dk_noalloc_scratch[DK_NOALLOC_SCRATCH_BYTES];
+
+static void* noalloc_scratch_ptr(dk_status* st) {
+  // The symbol's device address, looked up once per device with that device
+  // current (a host-side use of the symbol itself would not be a device
+  // address).
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) {
+    *st = DK_ERR_UNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_dk_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_cuda_error(e, "cudaGetSymbolAddress");
+      *st = DK_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *st = DK_OK;
+  return ptrs[dev];
+}
+
+extern "C" dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint16_t* scales,
+                                                  const uint16_t* x, uint16_t* y, int M, int K,
+                                                  int B, int split_k, void* stream) {
+  dk_gemv_config c;
+  dk_gemv_config_init(&c);
+  c.version = 4;
+  c.split_k = split_k;
+  dk_status s = validate_config(c);
+  if (s != DK_OK) return s;
+  if (M < 0 || K < 0 || B < 0) return DK_ERR_INVALID_ARG;
+  const size_t need = dk_w4a16_workspace_bytes(M, K, B, &c);
+  if (need > (size_t)DK_NOALLOC_SCRATCH_BYTES) return DK_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  if (need > 0) {
+    scratch = noalloc_scratch_ptr(&s);
+    if (s != DK_OK) return s;
+  }
+  // The split-K path clears the arrival counters at the start of every call,
+  // so whatever the previous call left in the buffer does not matter.
+  return dk_w4a16_gemv(packed, scales, x, y, M, K, B, &c, scratch,
+                       need > 0 ? (size_t)DK_NOALLOC_SCRATCH_BYTES : 0, stream);
+}
+
 extern "C" int dk_last_kernel_stamp(int device) {
   int prev = -1;
   cudaGetDevice(&prev);

@@ -22,6 +22,7 @@ DK_ERR_WORKSPACE = 6
 
 DK_FLAG_PDL = 0x1
 DK_QUANT_TORCH_CUDA_SCALE = 0x1
+DK_NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 class GemvConfig(ctypes.Structure):
@@ -42,6 +43,7 @@ SIGNATURES = {
     "dk_gemv_config_init": (None, [ctypes.POINTER(GemvConfig)]),
     "dk_w4a16_workspace_bytes": (_SZ, [_I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "dk_w4a16_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, _SZ, _P]),
+    "dk_w4a16_gemv_splitk_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "dk_d2d_copy": (_I, [_P, _P, _SZ, _P]),
     "dk_stream_read": (_I, [_P, _P, _SZ, _I, _P]),
     "dk_stream_write": (_I, [_P, _SZ, _I, _P]),

@@ -102,6 +102,29 @@ DK_API dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales, co
                         uint16_t* y, int M, int K, int B, const dk_gemv_config* cfg,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Split-K (version 4) GEMV that allocates nothing and takes no workspace.
+ * No counterpart in the reference.  It is for callers that cannot allocate
+ * device memory where they call the GEMV -- inside an allocator callback, in
+ * a runtime that hands out every buffer itself, or in code that must not
+ * touch the allocator on the decode path -- yet still want the split-K
+ * kernel.  Its scratch is one fixed buffer of DK_NOALLOC_SCRATCH_BYTES
+ * (8 MiB) compiled into the library, held on every GPU that loads the library
+ * until the process exits; the caller passes only inputs and outputs.
+ *  - Problems whose split-K workspace (dk_w4a16_workspace_bytes with
+ *    version 4) exceeds the buffer return DK_ERR_WORKSPACE.  Batches run in
+ *    passes of 8 rows, so the limit is M * (K/128) * 4 bytes plus a few KB of
+ *    counters for B >= 8 (e.g. M * K <= ~250M weights at B = 1).
+ *  - The first call on a device looks up the buffer's device address with that
+ *    device current; make that first call before any stream capture.
+ *  - All calls share the one buffer per device: calls that can overlap on the
+ *    GPU (different streams without ordering) race and must not be issued.
+ *    Each call clears what has to start at zero.
+ * Same results, bit for bit, as dk_w4a16_gemv with version 4. */
+#define DK_NOALLOC_SCRATCH_BYTES (8u << 20)
+DK_API dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint16_t* scales,
+                                              const uint16_t* x, uint16_t* y, int M, int K, int B,
+                                              int split_k, void* stream);
+
 /* STREAM-style HBM probes (gemv_w4a16.h:39-43).  `bytes` must be a multiple
  * of 16 and the pointers 16-byte aligned.  dk_stream_read writes one float
  * partial sum per block (blocks <= 0 picks dk_stream_recommended_blocks). */
