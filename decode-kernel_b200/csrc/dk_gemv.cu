@@ -499,17 +499,23 @@ constexpr int kStrip = 128;                             // bytes per swizzle str
 constexpr int kStripsPerChunk = kRowBytes / kStrip;     // 16
 constexpr int kMaxStages = 6;
 constexpr int kMinStages = 2;
-// Warp w handles groups w and w + 16 of every stage: class w of the canonical
-// order (G mod 16 == w), in ascending G.
-constexpr int kConsumerWarps = 16;
-constexpr int kGroupsPerWarp = kChunkGroups / kConsumerWarps;  // 2
-constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + 1 producer warp
+// Consumer warps: 16 (one CTA per SM, deepest ring) or 8 (a CTA small enough
+// that two fit on an SM, so a GEMV launched behind this one with PDL streams
+// its weights while this one computes).  Warp w handles groups w, w + NCW, ...
+// of every stage; group gi is class gi mod 16 of the canonical order, so with
+// 16 warps warp w owns class w and with 8 warps classes w and w + 8.
+template <int NCW>
+struct Consumers {
+  static constexpr int kWarps = NCW;
+  static constexpr int kThreads = NCW * 32;
+  static constexpr int kGroupsPerWarp = kChunkGroups / NCW;   // 2 or 4
+  static constexpr int kClassesPerWarp = kClasses / NCW;       // 1 or 2
+};
 constexpr int kXsMaxBytes = 68 * 1024;
-constexpr int kXsMaxChunksPerThread =
-    (kXsMaxBytes / 16 + kConsumerThreads - 1) / kConsumerThreads;
-constexpr int kSmemBudget = 220 * 1024;
 constexpr int kSmemCap = 227 * 1024;  // per-CTA opt-in maximum on sm_100
+// Shared-memory budget per CTA: the whole SM for 16 warps, half of it (minus
+// the per-CTA reserve) for 8 warps.
+__host__ __device__ constexpr int smem_budget(int ncw) { return ncw == 16 ? 220 * 1024 : 110 * 1024; }
 
 __host__ __device__ constexpr int stage_bytes(bool tmap) {
   return tmap ? kStageBytesTma : kStageBytesBulk;
@@ -528,7 +534,7 @@ __host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_b
   L.xs_off = off;
   off += (xs_bytes + 127) / 128 * 128;
   L.red_off = off;
-  off += 2 * kConsumerWarps * 16 * 8 * nt * (int)sizeof(float);
+  off += 2 * kClasses * 16 * 8 * nt * (int)sizeof(float);
   L.bar_off = off;
   off += (2 * kMaxStages + 5) * 8 + 16;  // full, empty, x, red_full[2], red_free[2], flag
   L.total = off;
@@ -639,10 +645,16 @@ __device__ __forceinline__ void fetch_x(const GemvParams& p, uint32_t xs, uint64
   }
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP>
-__global__ void __launch_bounds__(v5::kThreads, 1)
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
+__global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     k_stream(const __grid_constant__ CUtensorMap tmap, GemvParams p) {
   using namespace v5;
+  using CW = Consumers<NCW>;
+  constexpr int kConsumerWarps = CW::kWarps;
+  constexpr int kConsumerThreads = CW::kThreads;
+  constexpr int kGroupsPerWarp = CW::kGroupsPerWarp;
+  constexpr int kAcc = CW::kClassesPerWarp;
+  constexpr int kXsMaxChunksPerThread = (kXsMaxBytes / 16 + kConsumerThreads - 1) / kConsumerThreads;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int kStageBytes = stage_bytes(TMAP);
   constexpr int W = 8 * NT;  // output columns per tile row in the reduction buffer
@@ -803,9 +815,12 @@ __global__ void __launch_bounds__(v5::kThreads, 1)
   const uint32_t sc_a = ra * kScaleRowStride + warp * 2, sc_b = rb * kScaleRowStride + warp * 2;
   const uint32_t xq = xs + bb * xrow + 16 * c;  // + 256 G + 64 t
 
-  float acc[NT][4];
+  // acc[a]: this warp's class warp + a * NCW.
+  float acc[kAcc][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int a = 0; a < kAcc; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
 
   // Bulk path: scales from global memory, loaded one stage ahead.
   float sn[kGroupsPerWarp][2];
@@ -835,33 +850,45 @@ __global__ void __launch_bounds__(v5::kThreads, 1)
     nxt.next(nk, stages);
     if (!TMAP && s + 1 < total) load_scales(nxt);
 
-    if (mbar_wait_bounded(&full[cur.slot], cur.round & 1, abort_flag)) {
+    // Pull this warp's fragments (and the stage's scales) into registers and
+    // hand the slot back before computing, so the ring refills while the
+    // warps do the math.
+    uint4 wfa[kGroupsPerWarp], wfb[kGroupsPerWarp];
+    const bool have = mbar_wait_bounded(&full[cur.slot], cur.round & 1, abort_flag);
+    if (have) {
       const uint32_t st = ring + cur.slot * kStageBytes;
       const uint32_t sst = scs + cur.slot * kStageScaleBytes;
 #pragma unroll
       for (int j = 0; j < kGroupsPerWarp; ++j) {
-        const int gi = warp + j * kConsumerWarps;
-        if (gi < cg) {
-          const int G = cur.chunk * kChunkGroups + gi;
-          const uint4 wa = lds128(st + offa[j]);
-          const uint4 wb = lds128(st + offb[j]);
+        if (warp + j * kConsumerWarps < cg) {
+          wfa[j] = lds128(st + offa[j]);
+          wfb[j] = lds128(st + offb[j]);
           if constexpr (TMAP) {
             sc[j][0] = lds_half(sst + sc_a + j * 2 * kConsumerWarps);
             sc[j][1] = lds_half(sst + sc_b + j * 2 * kConsumerWarps);
           }
-          float d[NT][4];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-          if constexpr (XS)
-            group_mma_xs(wa, wb, xq + 256u * G, d[0]);
-          else
-            group_mma_gx<NT>(wa, wb, p.x, p.K, p.B, G * kGroup + 32 * c, g, d);
-          scale_accumulate<NT>(acc, d, sc[j][0], sc[j][1]);
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[cur.slot]);
+    if (have) {
+#pragma unroll
+      for (int j = 0; j < kGroupsPerWarp; ++j) {
+        const int gi = warp + j * kConsumerWarps;
+        if (gi < cg) {
+          const int G = cur.chunk * kChunkGroups + gi;
+          float d[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+          if constexpr (XS)
+            group_mma_xs(wfa[j], wfb[j], xq + 256u * G, d[0]);
+          else
+            group_mma_gx<NT>(wfa[j], wfb[j], p.x, p.K, p.B, G * kGroup + 32 * c, g, d);
+          scale_accumulate<NT>(acc[j % kAcc], d, sc[j][0], sc[j][1]);
+        }
+      }
+    }
 
     if (cur.chunk == nk - 1) {
       // Tile complete.  Each warp stores its partials (class = warp); warp
@@ -869,25 +896,28 @@ __global__ void __launch_bounds__(v5::kThreads, 1)
       // others move on.  Two buffers; a buffer is rewritten only after the
       // reducer two tiles back has released it.
       const int t = cur.tile, rs = t & 1;
-      float* rt = red + rs * kConsumerWarps * 16 * W;
+      float* rt = red + rs * kClasses * 16 * W;
       if (t >= 2) mbar_wait_bounded(&red_free[rs], ((t >> 1) - 1) & 1, abort_flag);
-      float* mine = rt + warp * 16 * W;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        mine[ra * W + nt * 8 + 2 * c] = acc[nt][0];
-        mine[ra * W + nt * 8 + 2 * c + 1] = acc[nt][1];
-        mine[rb * W + nt * 8 + 2 * c] = acc[nt][2];
-        mine[rb * W + nt * 8 + 2 * c + 1] = acc[nt][3];
+      for (int a = 0; a < kAcc; ++a) {
+        float* mine = rt + (warp + a * NCW) * 16 * W;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mine[ra * W + nt * 8 + 2 * c] = acc[a][nt][0];
+          mine[ra * W + nt * 8 + 2 * c + 1] = acc[a][nt][1];
+          mine[rb * W + nt * 8 + 2 * c] = acc[a][nt][2];
+          mine[rb * W + nt * 8 + 2 * c + 1] = acc[a][nt][3];
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[rs]);
-      if (warp == (t & (kConsumerWarps - 1))) {
+      if (warp == t % kConsumerWarps) {
         if (mbar_wait_bounded(&red_full[rs], (t >> 1) & 1, abort_flag)) {
           for (int o = lane; o < 16 * W; o += 32) {
             const int r = o / W, b = o % W;
             float sum = 0.f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) sum = __fadd_rn(sum, rt[w * 16 * W + o]);
+            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, rt[w * 16 * W + o]);
             if (r < rows && b < p.B) p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
           }
         }
@@ -895,7 +925,9 @@ __global__ void __launch_bounds__(v5::kThreads, 1)
         if (lane == 0) mbar_arrive(&red_free[rs]);
       }
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      for (int a = 0; a < kAcc; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
     }
     cur = nxt;
   }
@@ -1011,29 +1043,54 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
   return true;
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP>
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
 dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t st, bool pdl) {
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
   while (p.stages > v5::kMinStages &&
-         v5::layout(NT, TMAP, p.stages, p.xs_bytes).total > v5::kSmemBudget)
+         v5::layout(NT, TMAP, p.stages, p.xs_bytes).total > v5::smem_budget(NCW))
     --p.stages;
   const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes).total;
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
-  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP>, v5::kSmemCap, smem_done);
+  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
   const int grid = std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
-  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP>, dim3(grid), dim3(v5::kThreads), smem,
-                st, pdl, tmap, p);
+  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW>, dim3(grid), dim3(NCW * 32 + 32),
+                smem, st, pdl, tmap, p);
+}
+
+// 8 consumer warps (two CTAs per SM) while a CTA's share of the weights is
+// small -- then a CTA's life is dominated by latency and overlapping the next
+// GEMV pays most -- and while the 8-warp layout keeps at least 2 stages in
+// half of the SM's shared memory; 16 warps otherwise.
+template <int NT, bool XS, bool TMAP>
+bool use_coresident(const GemvParams& p) {
+#if defined(DK_V5_FORCE_NCW)
+  return DK_V5_FORCE_NCW == 8;
+#else
+  const int grid = std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
+  const size_t cta_bytes = ((size_t)p.M + grid - 1) / grid * (size_t)p.K / 2;
+  const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
+  return NT == 1 && XS && cta_bytes <= 160 * 1024 &&
+         v5::layout(NT, TMAP, v5::kMinStages, xs).total <= v5::smem_budget(8);
+#endif
+}
+
+template <int NT, int STAMP, bool XS, bool TMAP>
+dk_status launch_stream_w(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
+                          bool pdl) {
+  if (use_coresident<NT, XS, TMAP>(p))
+    return launch_stream_cfg<NT, STAMP, XS, TMAP, 8>(p, tmap, st, pdl);
+  return launch_stream_cfg<NT, STAMP, XS, TMAP, 16>(p, tmap, st, pdl);
 }
 
 template <int NT, int STAMP, bool TMAP>
 dk_status launch_stream_x(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
                           bool pdl) {
   if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
-    return launch_stream_cfg<1, STAMP, true, TMAP>(p, tmap, st, pdl);
-  return launch_stream_cfg<NT, STAMP, false, TMAP>(p, tmap, st, pdl);
+    return launch_stream_w<1, STAMP, true, TMAP>(p, tmap, st, pdl);
+  return launch_stream_w<NT, STAMP, false, TMAP>(p, tmap, st, pdl);
 }
 
 template <int NT, int STAMP>
