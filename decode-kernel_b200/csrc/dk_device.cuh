@@ -131,6 +131,11 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
+// Data another grid may have just written (x after a PDL wait): L2 only.
+__device__ __forceinline__ uint4 ldcg128(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+
 // Re-read data (x, scales): default caching so other warps hit L1.
 __device__ __forceinline__ uint4 ldg_keep(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));

@@ -474,13 +474,13 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
 // halves of the banks, so every fragment load is conflict-free.  (The padded
 // bulk layout is conflict-free with the identity mapping.)
 //
-// Activations: when the pass's x rows fit in kXsMaxBytes the producer copies
-// them once into shared memory (after the PDL wait -- x may be the previous
-// kernel's output; each batch row padded by 64 bytes) and the consumers
-// rearrange every 128-k group so that a group's B fragments are four
+// Activations: when the pass's x rows fit in kXsMaxBytes the consumers load
+// them once (after the PDL wait -- x may be the previous kernel's output) and
+// store every 128-k group rearranged so that a group's B fragments are four
 // conflict-free 128-bit loads: the pairs of word t for quad lane c sit at
-// 16 * (4t + c).  Larger x is read from global memory per group.  Batch lanes
-// past B read batch row B-1 (their columns are discarded).
+// 16 * (4t + c); each batch row is padded by 64 bytes.  Larger x is read from
+// global memory per group.  Batch lanes past B read batch row B-1 (their
+// columns are discarded).
 //
 // Tile results: every consumer warp stores its partial sums; one warp per tile
 // (rotating) adds the 16 classes in order and writes y while the others move
@@ -536,7 +536,7 @@ __host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_b
   L.red_off = off;
   off += 2 * kClasses * 16 * 8 * nt * (int)sizeof(float);
   L.bar_off = off;
-  off += (2 * kMaxStages + 5) * 8 + 16;  // full, empty, x, red_full[2], red_free[2], flag
+  off += (2 * kMaxStages + 4) * 8 + 16;  // full, empty, red_full[2], red_free[2], flag
   L.total = off;
   return L;
 }
@@ -629,22 +629,6 @@ __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
   }
 }
 
-// Producer helper: copy this pass's x rows into padded shared rows.
-__device__ __forceinline__ void fetch_x(const GemvParams& p, uint32_t xs, uint64_t* xbar,
-                                        int lane) {
-  const uint32_t row_bytes = 2u * (uint32_t)p.K;
-  const uint32_t pieces = (row_bytes + 4095u) / 4096u;
-  if (lane == 0) mbar_arrive_expect_tx(xbar, row_bytes * (uint32_t)p.B);
-  __syncwarp();
-  const uint64_t keep = policy_evict_last();
-  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x);
-  for (uint32_t i = lane; i < pieces * (uint32_t)p.B; i += 32) {
-    const uint32_t b = i / pieces, o = (i % pieces) * 4096u;
-    bulk_g2s(xs + b * (uint32_t)v5::xs_row_stride(p.K) + o, src + (size_t)b * row_bytes + o,
-             min(4096u, row_bytes - o), xbar, keep);
-  }
-}
-
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
 __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     k_stream(const __grid_constant__ CUtensorMap tmap, GemvParams p) {
@@ -654,7 +638,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   constexpr int kConsumerThreads = CW::kThreads;
   constexpr int kGroupsPerWarp = CW::kGroupsPerWarp;
   constexpr int kAcc = CW::kClassesPerWarp;
-  constexpr int kXsMaxChunksPerThread = (kXsMaxBytes / 16 + kConsumerThreads - 1) / kConsumerThreads;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int kStageBytes = stage_bytes(TMAP);
   constexpr int W = 8 * NT;  // output columns per tile row in the reduction buffer
@@ -662,8 +645,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* xbar = empty + kMaxStages;
-  uint64_t* red_full = xbar + 1;      // [2]: all consumer warps stored a tile
+  uint64_t* red_full = empty + kMaxStages;  // [2]: all consumer warps stored a tile
   uint64_t* red_free = red_full + 2;  // [2]: the tile's reducer has read it
   volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + 2);
   float* red = reinterpret_cast<float*>(smem + L.red_off);
@@ -687,7 +669,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       mbar_init(&full[s], TMAP ? 33 : 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
-    mbar_init(xbar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&red_full[i], kConsumerWarps);
       mbar_init(&red_free[i], 1);
@@ -709,12 +690,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     StageCursor cur;
     int issued = 0;
     for (int s = 0; s < total; ++s) {
-      if (XS && s == prefill) {
-        // Weights for the first `prefill` stages are in flight; now wait for
-        // the predecessor grid and fetch x (it may be its output).
-        pdl_wait();
-        fetch_x(p, xs, xbar, lane);
-      }
       if (s >= stages && !mbar_wait_bounded(&empty[cur.slot], (cur.round - 1) & 1, abort_flag))
         break;
       const int trow = r0 + cur.tile * 16;
@@ -751,18 +726,12 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       issued = s + 1;
       cur.next(nk, stages);
     }
-    if (XS && prefill == total && total > 0) {
-      // Every stage fit in the first fill: x has not been fetched yet.
-      pdl_wait();
-      fetch_x(p, xs, xbar, lane);
-    }
     if (*abort_flag && lane == 0) {
       // Let copies already in flight land before the CTA's shared memory is
       // released (bounded as well, against a fresh clock).
       volatile int no_abort = 0;
       for (int s = max(0, issued - stages); s < issued; ++s)
         mbar_wait_bounded(&full[s % stages], (s / stages) & 1, &no_abort);
-      if (XS) mbar_wait_bounded(xbar, 0, &no_abort);
     }
     return;
   }
@@ -774,32 +743,21 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   const int bb = min(g, p.B - 1);  // batch row this lane feeds into the mma
   const int xrow = xs_row_stride(p.K);
   if (XS) {
-    // Rearrange each 128-k group of x: raw 16-byte chunk i holds k = 8i..8i+7,
-    // i.e. word t = i % 4 of quad lane c = i / 4; it moves, with its pairs
-    // (x0,x4),(x1,x5),(x2,x6),(x3,x7), to chunk 4t + c.  All chunks are read
-    // before any is written.
-    const bool ok = mbar_wait_bounded(xbar, 0, abort_flag);
-    const int nchunks = p.B * groups * 16;
-    uint4 v[kXsMaxChunksPerThread];
-    uint32_t dst[kXsMaxChunksPerThread];
-#pragma unroll
-    for (int u = 0; u < kXsMaxChunksPerThread; ++u) {
-      const int q = threadIdx.x + u * kConsumerThreads;
-      if (ok && q < nchunks) {
-        const int i = q & 15, blk = q >> 4;
-        const uint32_t base = xs + (blk / groups) * xrow + (blk % groups) * 256;
-        v[u] = lds128(base + 16 * i);
-        dst[u] = base + 16 * (4 * (i & 3) + (i >> 2));
-      }
-    }
-    named_barrier(1, kConsumerThreads);
-#pragma unroll
-    for (int u = 0; u < kXsMaxChunksPerThread; ++u) {
-      const int q = threadIdx.x + u * kConsumerThreads;
-      if (ok && q < nchunks) {
+    // Stage x: raw 16-byte chunk i of a row holds k = 8i..8i+7, i.e. word
+    // t = i % 4 of quad lane c = (i / 4) % 4 of group i / 16; it is stored,
+    // as pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7), at chunk 4t + c of its
+    // group.  Loads go through L2 only (x may have just been written by the
+    // predecessor grid; no L1 line from an earlier kernel is trusted).
+    const int cpr = p.K / 8;
+    for (int b = 0; b < p.B; ++b) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)b * p.K);
+      const uint32_t rowbase = xs + (uint32_t)(b * xrow);
+#pragma unroll 4
+      for (int i = threadIdx.x; i < cpr; i += kConsumerThreads) {
         uint32_t pr[4];
-        pair_x8(v[u], pr);
-        sts128(dst[u], pr);
+        pair_x8(ldcg128(src + i), pr);
+        const int ii = i & 15;
+        sts128(rowbase + (uint32_t)(i >> 4) * 256u + 16u * (4 * (ii & 3) + (ii >> 2)), pr);
       }
     }
     named_barrier(1, kConsumerThreads);
@@ -903,22 +861,27 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         float* mine = rt + (warp + a * NCW) * 16 * W;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          mine[ra * W + nt * 8 + 2 * c] = acc[a][nt][0];
-          mine[ra * W + nt * 8 + 2 * c + 1] = acc[a][nt][1];
-          mine[rb * W + nt * 8 + 2 * c] = acc[a][nt][2];
-          mine[rb * W + nt * 8 + 2 * c + 1] = acc[a][nt][3];
+          if (nt * 8 + 2 * c < p.B) {  // columns past B are never read
+            mine[ra * W + nt * 8 + 2 * c] = acc[a][nt][0];
+            mine[ra * W + nt * 8 + 2 * c + 1] = acc[a][nt][1];
+            mine[rb * W + nt * 8 + 2 * c] = acc[a][nt][2];
+            mine[rb * W + nt * 8 + 2 * c + 1] = acc[a][nt][3];
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[rs]);
       if (warp == t % kConsumerWarps) {
         if (mbar_wait_bounded(&red_full[rs], (t >> 1) & 1, abort_flag)) {
-          for (int o = lane; o < 16 * W; o += 32) {
-            const int r = o / W, b = o % W;
+          // Only the tile's real rows and batch columns.
+          const int nb = min(W, p.B);
+          for (int o = lane; o < rows * nb; o += 32) {
+            const int r = o / nb, b = o - r * nb;
+            const float* src = rt + r * W + b;
             float sum = 0.f;
 #pragma unroll
-            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, rt[w * 16 * W + o]);
-            if (r < rows && b < p.B) p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
+            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * W]);
+            p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
           }
         }
         __syncwarp();
