@@ -499,6 +499,7 @@ constexpr int kStrip = 128;                             // bytes per swizzle str
 constexpr int kStripsPerChunk = kRowBytes / kStrip;     // 16
 constexpr int kMaxStages = 6;
 constexpr int kMinStages = 2;
+constexpr int kStagesBeforeX = 2;  // weight stages issued before x is staged
 // Consumer warps: 16 (one CTA per SM, deepest ring) or 8 (a CTA small enough
 // that two fit on an SM, so a GEMV launched behind this one with PDL streams
 // its weights while this one computes).  Warp w handles groups w, w + NCW, ...
@@ -536,7 +537,7 @@ __host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_b
   L.red_off = off;
   off += 2 * kClasses * 16 * 8 * nt * (int)sizeof(float);
   L.bar_off = off;
-  off += (2 * kMaxStages + 4) * 8 + 16;  // full, empty, red_full[2], red_free[2], flag
+  off += (2 * kMaxStages + 5) * 8 + 16;  // full, empty, red_full[2], red_free[2], xready, flag
   L.total = off;
   return L;
 }
@@ -647,7 +648,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* red_full = empty + kMaxStages;  // [2]: all consumer warps stored a tile
   uint64_t* red_free = red_full + 2;  // [2]: the tile's reducer has read it
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + 2);
+  uint64_t* xready = red_free + 2;    // the consumers have staged x
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(xready + 1);
   float* red = reinterpret_cast<float*>(smem + L.red_off);
   const uint32_t ring = smem_u32(smem);
   const uint32_t scs = smem_u32(smem + L.sc_off);
@@ -673,6 +675,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       mbar_init(&red_full[i], kConsumerWarps);
       mbar_init(&red_free[i], 1);
     }
+    mbar_init(xready, 1);
     *abort_flag = 0;
     fence_barrier_init();
     if constexpr (TMAP) tma_prefetch_desc(&tmap);
@@ -686,10 +689,13 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     const uint64_t policy = policy_evict_first();
     const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(p.packed);
     const size_t row_bytes = (size_t)p.K / 2;
-    const int prefill = min(stages, total);
     StageCursor cur;
     int issued = 0;
     for (int s = 0; s < total; ++s) {
+      // x is loaded by the consumers while the first stages stream; holding
+      // the rest back until it has landed keeps those loads from queueing
+      // behind a full ring of weight copies.
+      if (XS && s == kStagesBeforeX && !mbar_wait_bounded(xready, 0, abort_flag)) break;
       if (s >= stages && !mbar_wait_bounded(&empty[cur.slot], (cur.round - 1) & 1, abort_flag))
         break;
       const int trow = r0 + cur.tile * 16;
@@ -761,6 +767,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       }
     }
     named_barrier(1, kConsumerThreads);
+    if (threadIdx.x == 0) mbar_arrive(xready);
   }
 
   // Per-thread offsets, fixed for the whole kernel.
