@@ -195,24 +195,40 @@ def dequantize_np(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
     return (q.reshape(m, k // GROUP_SIZE, GROUP_SIZE) * s[..., None]).reshape(m, k)
 
 
-def linear_fp32_np(x: np.ndarray, packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
-    """The reference's CPU path restated in numpy: materialise fp32 W, then
-    one fp32 matmul (BLAS, all threads numpy was started with)."""
+def linear_fp32_np(x: np.ndarray, packed: np.ndarray, scales: np.ndarray,
+                   threads: int | None = None) -> np.ndarray:
+    """The reference's CPU path restated in numpy: materialise fp32 W, then an
+    fp32 matmul (reference.py:17-26).  The rows are split over ``threads``
+    host threads (default: every core this process may run on); each thread
+    dequantizes its row block and multiplies it with one-thread BLAS, so the
+    whole host works on the dequantisation, which dominates at small batch."""
     xf = _as_f16_bits(x).view(np.float16).astype(np.float32)
     if xf.ndim == 1:
         xf = xf[None, :]
-    w = dequantize_np(packed, scales)
-    return xf @ w.T
+    m = packed.shape[0]
+    n = max(1, min(threads or cpu_threads(), m // 64 or 1))
+    if n == 1:
+        return xf @ dequantize_np(packed, scales).T
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    out = np.empty((xf.shape[0], m), dtype=np.float32)
+    bounds = [m * i // n for i in range(n + 1)]
+
+    def work(i: int) -> None:
+        a, b = bounds[i], bounds[i + 1]
+        out[:, a:b] = xf @ dequantize_np(packed[a:b], scales[a:b]).T
+
+    with threadpool_limits(1, user_api="blas"), ThreadPoolExecutor(n) as ex:
+        list(ex.map(work, range(n)))
+    return out
 
 
 def cpu_threads() -> int:
-    """Threads the BLAS in linear_fp32_np may use."""
+    """Host threads linear_fp32_np uses by default: the cores this process may
+    run on."""
     try:
-        from threadpoolctl import threadpool_info
-
-        n = [d.get("num_threads", 1) for d in threadpool_info() if d.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
