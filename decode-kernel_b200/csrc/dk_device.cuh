@@ -195,6 +195,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // try_wait with a suspend-time hint: a thread whose phase is not complete
 // sleeps (up to `ns`) instead of spinning through issue slots.
+// Non-blocking phase test.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Warp-uniform non-blocking test: lane 0 tests (acquire), the warp follows
+// it past a __syncwarp so every lane is ordered after the phase.
+__device__ __forceinline__ bool warp_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_test_wait(bar, parity) ? 1u : 0u;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
   uint32_t ok;
   asm volatile(

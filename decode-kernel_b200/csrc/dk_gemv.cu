@@ -482,9 +482,9 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
 // global memory per group.  Batch lanes past B read batch row B-1 (their
 // columns are discarded).
 //
-// Tile results: every consumer warp stores its partial sums; one warp per tile
-// (rotating) adds the 16 classes in order and writes y while the others move
-// on -- two buffers guarded by mbarriers, no CTA-wide barrier per tile.
+// Tile results: every consumer warp stores its partial sums and moves on; the
+// producer warp, which polls instead of blocking, adds the 16 classes in order
+// and writes y -- two buffers guarded by mbarriers, no CTA-wide barrier.
 // ---------------------------------------------------------------------------
 namespace v5 {
 constexpr int kChunkK = 4096;                   // k per stage
@@ -685,52 +685,98 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   pdl_trigger();
 
   if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
+    // ---------------- producer: weight stages and tile sums ----------------
+    // It never blocks: each pass issues the next stage if its slot is free
+    // and adds up the next tile if all consumer warps have stored it, so the
+    // consumers never wait on a reduction and a pending reduction never
+    // waits on a slot.
     const uint64_t policy = policy_evict_first();
     const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(p.packed);
     const size_t row_bytes = (size_t)p.K / 2;
     StageCursor cur;
-    int issued = 0;
-    for (int s = 0; s < total; ++s) {
-      // x is loaded by the consumers while the first stages stream; holding
-      // the rest back until it has landed keeps those loads from queueing
-      // behind a full ring of weight copies.
-      if (XS && s == kStagesBeforeX && !mbar_wait_bounded(xready, 0, abort_flag)) break;
-      if (s >= stages && !mbar_wait_bounded(&empty[cur.slot], (cur.round - 1) & 1, abort_flag))
-        break;
-      const int trow = r0 + cur.tile * 16;
-      const uint32_t dst = ring + cur.slot * kStageBytes;
-      if constexpr (TMAP) {
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
-          tma_load_3d(dst, &tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot], policy);
-        }
-        // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups) per
-        // cp.async.  K % 256 == 0 here, so scale rows are 4-byte aligned.
-        const uint32_t sdst = scs + cur.slot * kStageScaleBytes;
-        const int gbase = cur.chunk * kChunkGroups;
+    int issued = 0, reduced = 0;
+    uint64_t idle_since = 0;
+    while (issued < total || reduced < ntiles) {
+      bool progress = false;
+      if (issued < total) {
+        // x is loaded by the consumers while the first stages stream; holding
+        // the rest back until it has landed keeps those loads from queueing
+        // behind a full ring of weight copies.
+        bool go = !(XS && issued == kStagesBeforeX) || warp_test_wait(xready, 0);
+        if (go && issued >= stages) go = warp_test_wait(&empty[cur.slot], (cur.round - 1) & 1);
+        if (go) {
+          const int trow = r0 + cur.tile * 16;
+          const uint32_t dst = ring + cur.slot * kStageBytes;
+          if constexpr (TMAP) {
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
+              tma_load_3d(dst, &tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot],
+                          policy);
+            }
+            // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups)
+            // per cp.async.  K % 256 == 0 here, so scale rows are 4-byte
+            // aligned.
+            const uint32_t sdst = scs + cur.slot * kStageScaleBytes;
+            const int gbase = cur.chunk * kChunkGroups;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
-          if (trow + r < p.M && gbase + w2 < groups)
-            cp_async4(sdst + r * kScaleRowStride + w2 * 2,
-                      p.scales + (size_t)(trow + r) * groups + gbase + w2);
-        }
-        cp_async_mbar_arrive(&full[cur.slot]);
-      } else {
-        const int rows = min(16, r1 - trow);
-        const uint32_t bytes =
-            (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
-        if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
-        __syncwarp();
-        if (lane < rows) {
-          bulk_g2s(dst + lane * kPadRowStride,
-                   wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
-                   bytes, &full[cur.slot], policy);
+            for (int k = 0; k < 8; ++k) {
+              const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
+              if (trow + r < p.M && gbase + w2 < groups)
+                cp_async4(sdst + r * kScaleRowStride + w2 * 2,
+                          p.scales + (size_t)(trow + r) * groups + gbase + w2);
+            }
+            cp_async_mbar_arrive(&full[cur.slot]);
+          } else {
+            const int rows = min(16, r1 - trow);
+            const uint32_t bytes =
+                (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
+            if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
+            __syncwarp();
+            if (lane < rows) {
+              bulk_g2s(dst + lane * kPadRowStride,
+                       wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
+                       bytes, &full[cur.slot], policy);
+            }
+          }
+          ++issued;
+          cur.next(nk, stages);
+          progress = true;
         }
       }
-      issued = s + 1;
-      cur.next(nk, stages);
+      if (reduced < ntiles && warp_test_wait(&red_full[reduced & 1], (reduced >> 1) & 1)) {
+        // Tile `reduced`: the 16 class partials of every real row and batch
+        // column, added in class order.
+        const float* rt = red + (reduced & 1) * kClasses * 16 * W;
+        const int trow = r0 + reduced * 16;
+        const int rows = min(16, r1 - trow);
+        const int nb = min(W, p.B);
+        for (int o = lane; o < rows * nb; o += 32) {
+          const int r = o / nb, b = o - r * nb;
+          const float* src = rt + r * W + b;
+          float sum = 0.f;
+#pragma unroll
+          for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * W]);
+          p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_free[reduced & 1]);
+        ++reduced;
+        progress = true;
+      }
+      if (progress) {
+        idle_since = 0;
+      } else {
+        if (*abort_flag) break;
+        const uint64_t now = globaltimer_ns();
+        if (idle_since == 0) {
+          idle_since = now;
+        } else if (now - idle_since > kWaitLimitNs) {
+          if (lane == 0) atomicExch(&g_dk_device_error, kDevWaitTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
     }
     if (*abort_flag && lane == 0) {
       // Let copies already in flight land before the CTA's shared memory is
@@ -856,10 +902,9 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     }
 
     if (cur.chunk == nk - 1) {
-      // Tile complete.  Each warp stores its partials (class = warp); warp
-      // (tile % 16) sums the 16 classes in order and writes y, while the
-      // others move on.  Two buffers; a buffer is rewritten only after the
-      // reducer two tiles back has released it.
+      // Tile complete: each warp stores its class partials and moves on; the
+      // producer warp adds them up.  Two buffers; a buffer is rewritten only
+      // after the producer has read the tile two back.
       const int t = cur.tile, rs = t & 1;
       float* rt = red + rs * kClasses * 16 * W;
       if (t >= 2) mbar_wait_bounded(&red_free[rs], ((t >> 1) - 1) & 1, abort_flag);
@@ -878,22 +923,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[rs]);
-      if (warp == t % kConsumerWarps) {
-        if (mbar_wait_bounded(&red_full[rs], (t >> 1) & 1, abort_flag)) {
-          // Only the tile's real rows and batch columns.
-          const int nb = min(W, p.B);
-          for (int o = lane; o < rows * nb; o += 32) {
-            const int r = o / nb, b = o - r * nb;
-            const float* src = rt + r * W + b;
-            float sum = 0.f;
-#pragma unroll
-            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * W]);
-            p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&red_free[rs]);
-      }
 #pragma unroll
       for (int a = 0; a < kAcc; ++a)
 #pragma unroll
@@ -1050,8 +1079,10 @@ bool use_coresident(const GemvParams& p) {
 template <int NT, int STAMP, bool XS, bool TMAP>
 dk_status launch_stream_w(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
                           bool pdl) {
-  if (use_coresident<NT, XS, TMAP>(p))
-    return launch_stream_cfg<NT, STAMP, XS, TMAP, 8>(p, tmap, st, pdl);
+  if constexpr (NT == 1 && XS) {
+    if (use_coresident<NT, XS, TMAP>(p))
+      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8>(p, tmap, st, pdl);
+  }
   return launch_stream_cfg<NT, STAMP, XS, TMAP, 16>(p, tmap, st, pdl);
 }
 
