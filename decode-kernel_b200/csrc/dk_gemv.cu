@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
 //
 // Tile results: every consumer warp stores its partial sums and moves on; the
 // producer warp, which polls instead of blocking, adds the 16 classes in order
-// and writes y -- two buffers guarded by mbarriers, no CTA-wide barrier.
+// and writes y -- kRedBufs buffers guarded by mbarriers, no CTA-wide barrier.
 // ---------------------------------------------------------------------------
 namespace v5 {
 constexpr int kChunkK = 4096;                   // k per stage
@@ -527,7 +527,14 @@ struct Layout {
   int sc_off, xs_off, red_off, bar_off, total;
 };
 
-__host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_bytes) {
+// Tile partial sums: kRedBufs buffers of [class][tile row][red_cols] floats,
+// so a consumer warp reaching the end of a tile never waits for the producer
+// to have added up the tile before last.  One n-tile keeps only the batch
+// columns that exist (rounded up to the even pair a quad lane stores).
+constexpr int kRedBufs = 4;
+__host__ __device__ inline int red_cols(int nt, int B) { return nt == 1 ? ((B + 1) & ~1) : 8 * nt; }
+
+__host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_bytes, int nbp) {
   Layout L;
   int off = stages * stage_bytes(tmap);
   L.sc_off = off;
@@ -535,9 +542,9 @@ __host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_b
   L.xs_off = off;
   off += (xs_bytes + 127) / 128 * 128;
   L.red_off = off;
-  off += 2 * kClasses * 16 * 8 * nt * (int)sizeof(float);
+  off += kRedBufs * kClasses * 16 * nbp * (int)sizeof(float);
   L.bar_off = off;
-  off += (2 * kMaxStages + 5) * 8 + 16;  // full, empty, red_full[2], red_free[2], xready, flag
+  off += (2 * kMaxStages + 2 * kRedBufs + 1) * 8 + 16;  // full, empty, red_full, red_free, xready, flag
   L.total = off;
   return L;
 }
@@ -641,14 +648,15 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   constexpr int kAcc = CW::kClassesPerWarp;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int kStageBytes = stage_bytes(TMAP);
-  constexpr int W = 8 * NT;  // output columns per tile row in the reduction buffer
+  constexpr int W = 8 * NT;  // mma output columns per tile row
   const int stages = p.stages;
-  const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0);
+  const int nbp = red_cols(NT, p.B);
+  const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0, nbp);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* red_full = empty + kMaxStages;  // [2]: all consumer warps stored a tile
-  uint64_t* red_free = red_full + 2;  // [2]: the tile's reducer has read it
-  uint64_t* xready = red_free + 2;    // the consumers have staged x
+  uint64_t* red_full = empty + kMaxStages;    // [kRedBufs]: all consumer warps stored a tile
+  uint64_t* red_free = red_full + kRedBufs;   // [kRedBufs]: the producer has read it
+  uint64_t* xready = red_free + kRedBufs;     // the consumers have staged x
   volatile int* abort_flag = reinterpret_cast<volatile int*>(xready + 1);
   float* red = reinterpret_cast<float*>(smem + L.red_off);
   const uint32_t ring = smem_u32(smem);
@@ -671,7 +679,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
       mbar_init(&full[s], TMAP ? 33 : 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kRedBufs; ++i) {
       mbar_init(&red_full[i], kConsumerWarps);
       mbar_init(&red_free[i], 1);
     }
@@ -743,23 +751,24 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
           progress = true;
         }
       }
-      if (reduced < ntiles && warp_test_wait(&red_full[reduced & 1], (reduced >> 1) & 1)) {
+      if (reduced < ntiles &&
+          warp_test_wait(&red_full[reduced % kRedBufs], (reduced / kRedBufs) & 1)) {
         // Tile `reduced`: the 16 class partials of every real row and batch
         // column, added in class order.
-        const float* rt = red + (reduced & 1) * kClasses * 16 * W;
+        const float* rt = red + (reduced % kRedBufs) * kClasses * 16 * nbp;
         const int trow = r0 + reduced * 16;
         const int rows = min(16, r1 - trow);
         const int nb = min(W, p.B);
         for (int o = lane; o < rows * nb; o += 32) {
           const int r = o / nb, b = o - r * nb;
-          const float* src = rt + r * W + b;
+          const float* src = rt + r * nbp + b;
           float sum = 0.f;
 #pragma unroll
-          for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * W]);
+          for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
           p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&red_free[reduced & 1]);
+        if (lane == 0) mbar_arrive(&red_free[reduced % kRedBufs]);
         ++reduced;
         progress = true;
       }
@@ -903,21 +912,22 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
 
     if (cur.chunk == nk - 1) {
       // Tile complete: each warp stores its class partials and moves on; the
-      // producer warp adds them up.  Two buffers; a buffer is rewritten only
-      // after the producer has read the tile two back.
-      const int t = cur.tile, rs = t & 1;
-      float* rt = red + rs * kClasses * 16 * W;
-      if (t >= 2) mbar_wait_bounded(&red_free[rs], ((t >> 1) - 1) & 1, abort_flag);
+      // producer warp adds them up.  A buffer is rewritten only after the
+      // producer has read the tile kRedBufs back.
+      const int t = cur.tile, rs = t % kRedBufs;
+      float* rt = red + rs * kClasses * 16 * nbp;
+      if (t >= kRedBufs)
+        mbar_wait_bounded(&red_free[rs], ((t / kRedBufs) - 1) & 1, abort_flag);
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) {
-        float* mine = rt + (warp + a * NCW) * 16 * W;
+        float* mine = rt + (warp + a * NCW) * 16 * nbp;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt * 8 + 2 * c < p.B) {  // columns past B are never read
-            mine[ra * W + nt * 8 + 2 * c] = acc[a][nt][0];
-            mine[ra * W + nt * 8 + 2 * c + 1] = acc[a][nt][1];
-            mine[rb * W + nt * 8 + 2 * c] = acc[a][nt][2];
-            mine[rb * W + nt * 8 + 2 * c + 1] = acc[a][nt][3];
+            mine[ra * nbp + nt * 8 + 2 * c] = acc[a][nt][0];
+            mine[ra * nbp + nt * 8 + 2 * c + 1] = acc[a][nt][1];
+            mine[rb * nbp + nt * 8 + 2 * c] = acc[a][nt][2];
+            mine[rb * nbp + nt * 8 + 2 * c + 1] = acc[a][nt][3];
           }
         }
       }
@@ -1048,9 +1058,10 @@ dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t 
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
   while (p.stages > v5::kMinStages &&
-         v5::layout(NT, TMAP, p.stages, p.xs_bytes).total > v5::smem_budget(NCW))
+         v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total >
+             v5::smem_budget(NCW))
     --p.stages;
-  const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes).total;
+  const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total;
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
@@ -1072,7 +1083,8 @@ bool use_coresident(const GemvParams& p) {
   const size_t cta_bytes = ((size_t)p.M + grid - 1) / grid * (size_t)p.K / 2;
   const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   return NT == 1 && XS && cta_bytes <= 160 * 1024 &&
-         v5::layout(NT, TMAP, v5::kMinStages, xs).total <= v5::smem_budget(8);
+         v5::layout(NT, TMAP, v5::kMinStages, xs, v5::red_cols(NT, p.B)).total <=
+             v5::smem_budget(8);
 #endif
 }
 
