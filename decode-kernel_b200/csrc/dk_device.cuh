@@ -236,11 +236,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-#ifdef DK_DEVICE_GLOBALS
-// Every wait in this library is bounded: 2 s of wall clock.  A wait that runs
-// out records kDevWaitTimeout in g_dk_device_error, raises the CTA's abort
-// flag (so every other wait in the CTA returns at once) and returns false.
+// Every wait in this library is bounded: 2 s of wall clock.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+#ifdef DK_DEVICE_GLOBALS
+// A wait that runs out records kDevWaitTimeout in g_dk_device_error, raises
+// the CTA's abort flag (so every other wait in the CTA returns at once) and
+// returns false.
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag) {

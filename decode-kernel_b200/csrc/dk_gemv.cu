@@ -50,17 +50,74 @@
 
 namespace dk {
 
+// Where v5 puts y (the other versions write fp16 y only).
+enum OutMode : int {
+  kOutHalf = 0,      // fp16 y [B, M]
+  kOutFloat = 1,     // fp32 dst[0] [B, M]
+  kOutRowShard = 2,  // fp16 into every rank's dst[g] [B, ld] at columns col0 + m
+  kOutKShard = 3,    // fp32 partial into every rank's dst[g] [world][B][M], slot `rank`
+};
+constexpr int kMaxShards = DK_MAX_SHARDS;
+struct OutSpec {
+  int mode = kOutHalf;
+  int world = 1, rank = 0;
+  int ld = 0, col0 = 0;
+  void* dst[kMaxShards] = {};
+  unsigned* flags[kMaxShards] = {};  // shard modes: each rank's arrival counter
+  unsigned* done = nullptr;          // shard modes: this rank's finished-CTA counter
+};
+
 struct GemvParams {
   const uint32_t* packed;  // [M, K/8]
   const __half* scales;    // [M, K/128]
-  const __half* x;         // [B, K]
+  const __half* x;         // [B, ldx]
   __half* y;               // [B, M]
   int M, K, B;
+  int ldx;                 // row stride of x in elements (K, or more for a K slice)
   float* ws;               // v4: [K/128][B][M] fp32 per-group products
   unsigned* counters;      // v4: one arrival counter per 16-row tile
   int stages;              // v5: ring depth
   int xs_bytes;            // v5: bytes of x staged in shared memory (0 = none)
+  OutSpec out;             // v5: destination of y
 };
+
+// v5 result store for batch row b, output row m.
+__device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v) {
+  switch (p.out.mode) {
+    case kOutFloat:
+      static_cast<float*>(p.out.dst[0])[(size_t)b * p.M + m] = v;
+      break;
+    case kOutRowShard: {
+      const __half h = __float2half_rn(v);
+      for (int g = 0; g < p.out.world; ++g)
+        static_cast<__half*>(p.out.dst[g])[(size_t)b * p.out.ld + p.out.col0 + m] = h;
+      break;
+    }
+    case kOutKShard:
+      for (int g = 0; g < p.out.world; ++g)
+        static_cast<float*>(p.out.dst[g])[((size_t)p.out.rank * p.B + b) * p.M + m] = v;
+      break;
+    default:
+      p.y[(size_t)b * p.M + m] = __float2half_rn(v);
+  }
+}
+
+// Shard modes: once every CTA of this rank has stored its rows, count this
+// rank in on every rank's arrival counter (each call adds 1 per rank, so a
+// rank waits for world * calls).  Called by the one warp that wrote y.
+__device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
+  if (p.out.mode < kOutRowShard) return;
+  __threadfence_system();  // this lane's stores to every rank, before the count
+  __syncwarp();
+  if (lane == 0) {
+    const unsigned old = atomicAdd(p.out.done, 1u);
+    if (old == gridDim.x - 1) {
+      *p.out.done = 0;  // the next call on this stream starts from zero
+      __threadfence_system();
+      for (int g = 0; g < p.out.world; ++g) atomicAdd_system(p.out.flags[g], 1u);
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
 // Shared math
@@ -765,7 +822,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
-          p.y[(size_t)b * p.M + trow + r] = __float2half_rn(sum);
+          store_y(p, b, trow + r, sum);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_free[reduced % kRedBufs]);
@@ -787,12 +844,16 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         __nanosleep(64);
       }
     }
-    if (*abort_flag && lane == 0) {
-      // Let copies already in flight land before the CTA's shared memory is
-      // released (bounded as well, against a fresh clock).
-      volatile int no_abort = 0;
-      for (int s = max(0, issued - stages); s < issued; ++s)
-        mbar_wait_bounded(&full[s % stages], (s / stages) & 1, &no_abort);
+    if (*abort_flag) {
+      if (lane == 0) {
+        // Let copies already in flight land before the CTA's shared memory
+        // is released (bounded as well, against a fresh clock).
+        volatile int no_abort = 0;
+        for (int s = max(0, issued - stages); s < issued; ++s)
+          mbar_wait_bounded(&full[s % stages], (s / stages) & 1, &no_abort);
+      }
+    } else {
+      signal_shards(p, lane);
     }
     return;
   }
@@ -811,7 +872,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     // predecessor grid; no L1 line from an earlier kernel is trusted).
     const int cpr = p.K / 8;
     for (int b = 0; b < p.B; ++b) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)b * p.K);
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)b * p.ldx);
       const uint32_t rowbase = xs + (uint32_t)(b * xrow);
 #pragma unroll 4
       for (int i = threadIdx.x; i < cpr; i += kConsumerThreads) {
@@ -904,7 +965,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
           if constexpr (XS)
             group_mma_xs(wfa[j], wfb[j], xq + 256u * G, d[0]);
           else
-            group_mma_gx<NT>(wfa[j], wfb[j], p.x, p.K, p.B, G * kGroup + 32 * c, g, d);
+            group_mma_gx<NT>(wfa[j], wfb[j], p.x, p.ldx, p.B, G * kGroup + 32 * c, g, d);
           scale_accumulate<NT>(acc[j % kAcc], d, sc[j][0], sc[j][1]);
         }
       }
@@ -1183,9 +1244,12 @@ static dk_status validate_config(const dk_gemv_config& c) {
   if (c.split_k < 1 || c.split_k > 32) return DK_ERR_INVALID_ARG;
   if (c.warps_per_row < 1 || c.warps_per_row > 8) return DK_ERR_INVALID_ARG;
   if (c.warps_per_row > 1 && (c.version != 1 || c.reuse_weights)) return DK_ERR_INVALID_ARG;
-  if (c.flags & ~DK_FLAG_PDL) return DK_ERR_INVALID_ARG;
+  if (c.flags & ~(DK_FLAG_PDL | DK_FLAG_F32_OUT)) return DK_ERR_INVALID_ARG;
   return DK_OK;
 }
+
+// fp32 output exists on the v5 pipeline only.
+static bool f32_supported(const dk_gemv_config& c) { return c.reuse_weights || c.version == 5; }
 
 static int effective_split(int K, const dk_gemv_config& c) {
   if (c.reuse_weights || c.version != 4) return 1;
@@ -1213,8 +1277,11 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
   if (M == 0 || B == 0) return DK_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!y) return DK_ERR_INVALID_ARG;
+  const bool f32 = (c.flags & DK_FLAG_F32_OUT) != 0;
+  if (f32 && !f32_supported(c)) return DK_ERR_UNSUPPORTED;
   if (K == 0) {  // empty reduction: y = 0
-    const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)B * M * sizeof(uint16_t), st);
+    const size_t elem = f32 ? sizeof(float) : sizeof(uint16_t);
+    const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)B * M * elem, st);
     if (e != cudaSuccess) {
       set_cuda_error(e, "cudaMemsetAsync");
       return DK_ERR_CUDA;
@@ -1223,7 +1290,7 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
   }
   if (!packed || !scales || !x) return DK_ERR_INVALID_ARG;
   if (!aligned16(packed) || !aligned16(x) || (reinterpret_cast<uintptr_t>(scales) & 1u) ||
-      (reinterpret_cast<uintptr_t>(y) & 1u))
+      (reinterpret_cast<uintptr_t>(y) & (f32 ? 3u : 1u)))
     return DK_ERR_INVALID_ARG;
 
   const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
@@ -1255,7 +1322,12 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
     p.y = reinterpret_cast<__half*>(y) + (size_t)b0 * M;
     p.M = M;
     p.K = K;
+    p.ldx = K;
     p.B = std::min(step, B - b0);
+    if (f32) {
+      p.out.mode = kOutFloat;
+      p.out.dst[0] = reinterpret_cast<float*>(y) + (size_t)b0 * M;
+    }
     p.ws = partials;
     p.counters = counters;
     if (c.reuse_weights) {
@@ -1291,6 +1363,80 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
     if (s != DK_OK) return s;
   }
   return DK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Sharded GEMV (row-parallel and K-parallel): the v5 pipeline with its
+// epilogue storing into every rank's buffer and counting the rank in.
+// ---------------------------------------------------------------------------
+static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_gemv_config* cfg,
+                              cudaStream_t st) {
+  dk_gemv_config c;
+  dk_gemv_config_init(&c);
+  if (cfg) c = *cfg;
+  dk_status s = validate_config(c);
+  if (s != DK_OK) return s;
+  if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
+  if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
+      !g->done)
+    return DK_ERR_INVALID_ARG;
+  for (int i = 0; i < g->world; ++i)
+    if (!g->bufs[i] || !g->flags[i]) return DK_ERR_INVALID_ARG;
+  if (p.M <= 0 || p.K <= 0 || p.K % DK_GROUP_SIZE != 0 || p.B <= 0) return DK_ERR_INVALID_ARG;
+  if (p.B > kMaxBatchPerPass) return DK_ERR_UNSUPPORTED;
+  if (!p.packed || !p.scales || !p.x || !aligned16(p.packed) || !aligned16(p.x) ||
+      (reinterpret_cast<uintptr_t>(p.scales) & 1u) || p.ldx < p.K || p.ldx % 8 != 0)
+    return DK_ERR_INVALID_ARG;
+  p.out.world = g->world;
+  p.out.rank = g->rank;
+  for (int i = 0; i < g->world; ++i) {
+    p.out.dst[i] = g->bufs[i];
+    p.out.flags[i] = g->flags[i];
+  }
+  p.out.done = g->done;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  p.y = nullptr;
+  const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
+  return c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl)
+                         : launch_stream_nt<5>(p, st, pdl);
+}
+
+extern "C" dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_t* scales,
+                                            const uint16_t* x, int M_shard, int row0,
+                                            int M_total, int K, int B,
+                                            const dk_shard_group* group,
+                                            const dk_gemv_config* cfg, void* stream) {
+  if (M_shard <= 0 || row0 < 0 || M_total < row0 + M_shard) return DK_ERR_INVALID_ARG;
+  GemvParams p;
+  p.packed = reinterpret_cast<const uint32_t*>(packed);
+  p.scales = reinterpret_cast<const __half*>(scales);
+  p.x = reinterpret_cast<const __half*>(x);
+  p.M = M_shard;
+  p.K = K;
+  p.ldx = K;
+  p.B = B;
+  p.out.mode = kOutRowShard;
+  p.out.ld = M_total;
+  p.out.col0 = row0;
+  return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* scales,
+                                          const uint16_t* x, int ldx, int M, int K_shard, int B,
+                                          const dk_shard_group* group, const dk_gemv_config* cfg,
+                                          void* stream) {
+  GemvParams p;
+  p.packed = reinterpret_cast<const uint32_t*>(packed);
+  p.scales = reinterpret_cast<const __half*>(scales);
+  p.x = reinterpret_cast<const __half*>(x);
+  p.M = M;
+  p.K = K_shard;
+  p.ldx = ldx;
+  p.B = B;
+  p.out.mode = kOutKShard;
+  p.out.ld = M;
+  return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -1363,6 +1509,22 @@ extern "C" int dk_last_kernel_stamp(int device) {
   if (cudaMemcpyFromSymbol(&h, g_dk_kernel_stamp, sizeof(int)) != cudaSuccess) h = -1;
   if (device >= 0 && device != prev) cudaSetDevice(prev);
   return h;
+}
+
+int* dk::device_error_address() {
+  static std::mutex mu;
+  static int* cache[64] = {nullptr};
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_dk_device_error);
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "cudaGetSymbolAddress");
+    return nullptr;
+  }
+  if (dev >= 0 && dev < 64) cache[dev] = static_cast<int*>(p);
+  return static_cast<int*>(p);
 }
 
 extern "C" int dk_device_error(int device, int clear) {

@@ -1,6 +1,9 @@
 // dk_host.h -- host-side helpers shared by the library's translation units.
 #pragma once
 
+#include <algorithm>
+#include <cstdint>
+
 #include <cuda_runtime.h>
 
 #include "dk_w4a16.h"
@@ -16,6 +19,10 @@ int sm_count(int device);
 
 // Current device id.
 int current_device();
+
+// Device address of the device error word on the current device (defined in
+// dk_gemv.cu), for kernels of other translation units; nullptr on failure.
+int* device_error_address();
 
 inline dk_status check_launch(const char* where) {
   const cudaError_t e = cudaGetLastError();

@@ -1,0 +1,147 @@
+// dk_shard.cu -- the exchange side of the sharded GEMV: bounded arrival waits,
+// the K-parallel partial reduction, and the peer-memory plumbing (CUDA IPC
+// handles, mapped with lazy peer access over NVLink).
+//
+// The GEMV kernels themselves (dk_w4a16_gemv_rowshard / _kshard in
+// dk_gemv.cu) store their results into every rank's buffer and then add one
+// to every rank's arrival counter per call, after a system-scope fence.  The
+// waits here read the local counter with acquire semantics at system scope,
+// so everything the counted ranks stored before their fence is visible to the
+// work that follows on the stream.
+#include <cstring>
+
+#include "dk_device.cuh"
+#include "dk_host.h"
+
+namespace dk {
+namespace {
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// True once *flag >= target (wrap-safe); false after the wait bound, with the
+// timeout recorded in the device error word.
+__device__ bool wait_count(const unsigned* flag, unsigned target, int* err) {
+  if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(128);
+    if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(err, kDevWaitTimeout);
+      return false;
+    }
+  }
+}
+
+__global__ void k_shard_wait(const unsigned* flag, unsigned target, int* err) {
+  if (threadIdx.x == 0) wait_count(flag, target, err);
+}
+
+// y[i] = fp16(sum_r part[r][i]) in ascending r; part is [world][n].  The
+// partials were stored by other GPUs: read them from L2.
+__global__ void k_shard_reduce(const float* part, int world, int n, __half* y,
+                               const unsigned* flag, unsigned target, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = wait_count(flag, target, err) ? 1 : 0;
+  __syncthreads();
+  if (!ok) return;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < world; ++r) s = __fadd_rn(s, __ldcg(part + (size_t)r * n + i));
+    y[i] = __float2half_rn(s);
+  }
+}
+
+}  // namespace
+}  // namespace dk
+
+using namespace dk;
+
+extern "C" dk_status dk_shard_wait(const unsigned* flag, unsigned target, void* stream) {
+  if (!flag) return DK_ERR_INVALID_ARG;
+  int* err = device_error_address();
+  if (!err) return DK_ERR_CUDA;
+  k_shard_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, target, err);
+  return check_launch("k_shard_wait");
+}
+
+extern "C" dk_status dk_shard_reduce(const float* partials, int world, int M, int B, uint16_t* y,
+                                     const unsigned* flag, unsigned target, void* stream) {
+  if (!partials || !y || !flag || world < 1 || world > DK_MAX_SHARDS || M < 0 || B < 0)
+    return DK_ERR_INVALID_ARG;
+  const long long n = (long long)M * B;
+  if (n == 0) return DK_OK;
+  if (n > (1ll << 30)) return DK_ERR_UNSUPPORTED;
+  int* err = device_error_address();
+  if (!err) return DK_ERR_CUDA;
+  const int threads = 256;
+  const int blocks = (int)std::min<long long>((n + threads - 1) / threads, 4ll * sm_count(-1));
+  k_shard_reduce<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      partials, world, (int)n, reinterpret_cast<__half*>(y), flag, target, err);
+  return check_launch("k_shard_reduce");
+}
+
+extern "C" dk_status dk_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return DK_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "dk_peer_alloc");
+    if (*ptr) cudaFree(*ptr);
+    *ptr = nullptr;
+    return DK_ERR_CUDA;
+  }
+  return DK_OK;
+}
+
+extern "C" dk_status dk_peer_free(void* ptr) {
+  if (!ptr) return DK_OK;
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "dk_peer_free");
+    return DK_ERR_CUDA;
+  }
+  return DK_OK;
+}
+
+extern "C" dk_status dk_peer_export(const void* ptr, unsigned char* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == DK_PEER_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle) return DK_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "dk_peer_export");
+    return DK_ERR_CUDA;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  return DK_OK;
+}
+
+extern "C" dk_status dk_peer_import(const unsigned char* handle, void** ptr) {
+  if (!handle || !ptr) return DK_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "dk_peer_import");
+    *ptr = nullptr;
+    return DK_ERR_CUDA;
+  }
+  return DK_OK;
+}
+
+extern "C" dk_status dk_peer_close(void* ptr) {
+  if (!ptr) return DK_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) {
+    set_cuda_error(e, "dk_peer_close");
+    return DK_ERR_CUDA;
+  }
+  return DK_OK;
+}

@@ -21,8 +21,11 @@ DK_ERR_CUDA = 5
 DK_ERR_WORKSPACE = 6
 
 DK_FLAG_PDL = 0x1
+DK_FLAG_F32_OUT = 0x2
 DK_QUANT_TORCH_CUDA_SCALE = 0x1
 DK_NOALLOC_SCRATCH_BYTES = 8 << 20
+DK_MAX_SHARDS = 8
+DK_PEER_HANDLE_BYTES = 64
 
 
 class GemvConfig(ctypes.Structure):
@@ -37,6 +40,20 @@ class GemvConfig(ctypes.Structure):
     ]
 
 
+class ShardGroup(ctypes.Structure):
+    """struct dk_shard_group: this rank, the world size, every rank's result
+    buffer and arrival counter as mapped in this process, and this rank's own
+    finished-CTA counter."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int),
+        ("world", ctypes.c_int),
+        ("bufs", ctypes.c_void_p * DK_MAX_SHARDS),
+        ("flags", ctypes.c_void_p * DK_MAX_SHARDS),
+        ("done", ctypes.c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/dk_w4a16.h declares.
 _P, _I, _U, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_size_t
 SIGNATURES = {
@@ -44,6 +61,17 @@ SIGNATURES = {
     "dk_w4a16_workspace_bytes": (_SZ, [_I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "dk_w4a16_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, _SZ, _P]),
     "dk_w4a16_gemv_splitk_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "dk_w4a16_gemv_rowshard": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
+                                    ctypes.POINTER(GemvConfig), _P]),
+    "dk_w4a16_gemv_kshard": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
+                                  ctypes.POINTER(GemvConfig), _P]),
+    "dk_shard_wait": (_I, [_P, _U, _P]),
+    "dk_shard_reduce": (_I, [_P, _I, _I, _I, _P, _P, _U, _P]),
+    "dk_peer_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
+    "dk_peer_free": (_I, [_P]),
+    "dk_peer_export": (_I, [_P, ctypes.c_char_p]),
+    "dk_peer_import": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "dk_peer_close": (_I, [_P]),
     "dk_d2d_copy": (_I, [_P, _P, _SZ, _P]),
     "dk_stream_read": (_I, [_P, _P, _SZ, _I, _P]),
     "dk_stream_write": (_I, [_P, _SZ, _I, _P]),

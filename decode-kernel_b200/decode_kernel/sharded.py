@@ -1,0 +1,360 @@
+"""W4A16 layers sharded across the GPUs of one node, one process per GPU.
+
+Two layouts (the reference is single-GPU; these serve its 7B-stack and
+70B-layer configurations across 1/2/4/8 B200s):
+
+* ``RowParallelW4A16`` -- rank r owns the output rows
+  ``[r*M//G, (r+1)*M//G)`` (a contiguous slice of ``packed`` and ``scales``,
+  no repacking); ``x`` is replicated; every rank ends with the full ``y``.
+* ``KParallelW4A16`` -- rank r owns a group-aligned slice of K (copied once
+  into its own contiguous ``packed``/``scales``); every rank computes an fp32
+  partial ``[B, M]`` and every rank ends with the sum in rank order.
+
+``exchange="fused"`` (default) runs the exchange inside the GEMV: the kernel's
+epilogue stores its results straight into every rank's buffer over NVLink peer
+memory and counts the rank in on every rank's arrival counter
+(``dk_w4a16_gemv_rowshard`` / ``dk_w4a16_gemv_kshard``); a bounded wait
+(``dk_shard_wait`` / ``dk_shard_reduce``) then releases the stream.
+``exchange="nccl"`` runs the plain GEMV followed by torch.distributed
+collectives -- the baseline the fused path is measured against.
+
+Peer buffers are plain device allocations shared by CUDA IPC handles that the
+ranks swap over the process group.  ``PeerBuffers(..., emulate=G)`` instead
+keeps all G ranks' buffers in one process on one GPU, so the whole code path
+(every rank's kernel writing every rank's buffer, the counters, the waits) can
+be exercised without G GPUs: the ranks' kernels then run one after another on
+one stream, and no kernel ever waits for one that has not already finished.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import capi
+from .quantize import GROUP_SIZE
+
+__all__ = [
+    "PeerBuffers",
+    "RowParallelW4A16",
+    "KParallelW4A16",
+    "row_range",
+    "k_range",
+    "slice_rows",
+    "slice_k",
+]
+
+
+# --------------------------------------------------------------------------
+# Partitioning (host arithmetic; also what the CPU tests check)
+# --------------------------------------------------------------------------
+
+def row_range(M: int, world: int, rank: int) -> tuple[int, int]:
+    """Output rows [row0, row0 + rows) of ``rank``: balanced and contiguous."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    row0 = rank * M // world
+    return row0, (rank + 1) * M // world - row0
+
+
+def k_range(K: int, world: int, rank: int) -> tuple[int, int]:
+    """Reduction columns [k0, k0 + kn) of ``rank``: whole 128-wide groups,
+    balanced over the ranks (K // 128 need not divide by the world)."""
+    if K % GROUP_SIZE:
+        raise ValueError(f"K={K} is not a multiple of {GROUP_SIZE}")
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    groups = K // GROUP_SIZE
+    g0, g1 = rank * groups // world, (rank + 1) * groups // world
+    return g0 * GROUP_SIZE, (g1 - g0) * GROUP_SIZE
+
+
+def slice_rows(packed: torch.Tensor, scales: torch.Tensor, world: int, rank: int):
+    """(packed rows, scales rows, row0) of ``rank`` (views, contiguous)."""
+    row0, rows = row_range(packed.shape[0], world, rank)
+    return packed[row0:row0 + rows], scales[row0:row0 + rows], row0
+
+
+def slice_k(packed: torch.Tensor, scales: torch.Tensor, world: int, rank: int):
+    """(packed, scales, k0) of ``rank``'s K slice as new contiguous tensors."""
+    K = packed.shape[1] * 8
+    k0, kn = k_range(K, world, rank)
+    p = packed[:, k0 // 8:(k0 + kn) // 8].contiguous()
+    s = scales[:, k0 // GROUP_SIZE:(k0 + kn) // GROUP_SIZE].contiguous()
+    return p, s, k0
+
+
+# --------------------------------------------------------------------------
+# Peer memory
+# --------------------------------------------------------------------------
+
+class _DeviceArray:
+    """A raw device allocation described by __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape: Sequence[int], typestr: str):
+        self.__cuda_array_interface__ = {
+            "data": (int(ptr), False), "shape": tuple(shape), "typestr": typestr,
+            "strides": None, "version": 3,
+        }
+
+
+def _check(status: int, what: str) -> None:
+    capi.check(status, what)
+
+
+class PeerBuffers:
+    """Result buffers (two sets, used in turn) and arrival counters of every
+    rank, mapped in this process.
+
+    ``nbytes`` is the size of one result buffer.  With a process group each
+    process owns its own rank's memory and maps the others'; with
+    ``emulate=G`` one process owns all G ranks' memory on its one GPU.
+    """
+
+    def __init__(self, nbytes: int, group=None, emulate: Optional[int] = None):
+        self.lib = capi.load()
+        self.nbytes = int(nbytes)
+        self._owned: list[int] = []
+        self._mapped: list[int] = []
+        self.calls = 0
+        if emulate is not None:
+            self.world, self.rank, self.emulated = int(emulate), 0, True
+            if not 1 <= self.world <= capi.DK_MAX_SHARDS:
+                raise ValueError(f"world {self.world} outside 1..{capi.DK_MAX_SHARDS}")
+            self.bufs = [[self._alloc(self.nbytes) for _ in range(self.world)] for _ in range(2)]
+            self.flags = [self._alloc(16) for _ in range(self.world)]
+            self.dones = [self._alloc(16) for _ in range(self.world)]
+            return
+        import torch.distributed as dist
+
+        self.emulated = False
+        self.world = dist.get_world_size(group) if group is not None or dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if not 1 <= self.world <= capi.DK_MAX_SHARDS:
+            raise ValueError(f"world {self.world} outside 1..{capi.DK_MAX_SHARDS}")
+        mine = [self._alloc(self.nbytes), self._alloc(self.nbytes), self._alloc(16)]
+        self.dones = [self._alloc(16)]
+        if self.world == 1:
+            self.bufs = [[mine[0]], [mine[1]]]
+            self.flags = [mine[2]]
+            return
+        handles = []
+        for ptr in mine:
+            h = ctypes.create_string_buffer(capi.DK_PEER_HANDLE_BYTES)
+            _check(self.lib.dk_peer_export(ptr, h), "dk_peer_export")
+            handles.append(bytes(h.raw))
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        table = []
+        for r, hs in enumerate(everyone):
+            if r == self.rank:
+                table.append(mine)
+                continue
+            row = []
+            for h in hs:
+                p = ctypes.c_void_p()
+                _check(self.lib.dk_peer_import(h, ctypes.byref(p)), "dk_peer_import")
+                self._mapped.append(p.value)
+                row.append(p.value)
+            table.append(row)
+        self.bufs = [[table[r][0] for r in range(self.world)],
+                     [table[r][1] for r in range(self.world)]]
+        self.flags = [table[r][2] for r in range(self.world)]
+
+    def _alloc(self, n: int) -> int:
+        p = ctypes.c_void_p()
+        _check(self.lib.dk_peer_alloc(n, ctypes.byref(p)), "dk_peer_alloc")
+        self._owned.append(p.value)
+        return p.value
+
+    # Ranks this process acts for: all of them when emulating, else its own.
+    def local_ranks(self) -> list[int]:
+        return list(range(self.world)) if self.emulated else [self.rank]
+
+    def group(self, rank: int, which: int) -> capi.ShardGroup:
+        g = capi.ShardGroup()
+        g.rank, g.world = rank, self.world
+        for r in range(self.world):
+            g.bufs[r] = self.bufs[which][r]
+            g.flags[r] = self.flags[r]
+        g.done = self.dones[rank if self.emulated else 0]
+        return g
+
+    def view(self, rank: int, which: int, shape: Sequence[int], dtype: torch.dtype) -> torch.Tensor:
+        """``rank``'s buffer of set ``which`` as a tensor (no copy)."""
+        typestr = {torch.float16: "<f2", torch.float32: "<f4"}[dtype]
+        n = 1
+        for d in shape:
+            n *= int(d)
+        if n * torch.finfo(dtype).bits // 8 > self.nbytes:
+            raise ValueError("view larger than the peer buffer")
+        return torch.as_tensor(_DeviceArray(self.bufs[which][rank], shape, typestr),
+                               device=torch.device("cuda", torch.cuda.current_device()))
+
+    def begin(self) -> tuple[int, int]:
+        """Next call: (buffer set to write, arrival target to wait for)."""
+        which = self.calls & 1
+        self.calls += 1
+        return which, (self.calls * self.world) & 0xFFFFFFFF
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        for p in self._mapped:
+            self.lib.dk_peer_close(p)
+        for p in self._owned:
+            self.lib.dk_peer_free(p)
+        self._mapped, self._owned = [], []
+
+    def __del__(self):
+        try:
+            if self._owned or self._mapped:
+                self.close()
+        except Exception:
+            pass
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cfg(pdl: bool) -> capi.GemvConfig:
+    return capi.default_config(version=5, flags=capi.DK_FLAG_PDL if pdl else 0)
+
+
+# --------------------------------------------------------------------------
+# Layers
+# --------------------------------------------------------------------------
+
+class RowParallelW4A16:
+    """y[B, M] = x[B, K] . W^T with W's output rows split over the ranks.
+
+    ``packed``/``scales`` are the FULL tensors; each local rank keeps its rows
+    on the current GPU.  Call with the replicated x; returns the gathered
+    fp16 y on every rank (a view of a buffer the call after next reuses).
+    """
+
+    def __init__(self, packed: torch.Tensor, scales: torch.Tensor, peers: PeerBuffers,
+                 max_batch: int = 1, exchange: str = "fused", group=None):
+        if exchange not in ("fused", "nccl"):
+            raise ValueError(exchange)
+        self.M, self.K = packed.shape[0], packed.shape[1] * 8
+        self.peers, self.exchange, self.group = peers, exchange, group
+        self.max_batch = int(max_batch)
+        if 2 * self.max_batch * self.M > peers.nbytes:
+            raise ValueError("peer buffers too small for [max_batch, M] fp16")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.shards = {}
+        for r in peers.local_ranks():
+            p, s, row0 = slice_rows(packed, scales, peers.world, r)
+            self.shards[r] = (p.to(dev).contiguous(), s.to(dev).contiguous(), row0)
+
+    def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        B = x.shape[0]
+        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
+            raise RuntimeError("x must be contiguous fp16 [B, K]")
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
+        if self.exchange == "nccl":
+            return self._nccl(x)
+        lib, st, cfg = self.peers.lib, _stream(), _cfg(pdl)
+        which, target = self.peers.begin()
+        for r, (p, s, row0) in self.shards.items():
+            g = self.peers.group(r, which)
+            _check(lib.dk_w4a16_gemv_rowshard(p.data_ptr(), s.data_ptr(), x.data_ptr(),
+                                              p.shape[0], row0, self.M, self.K, B,
+                                              ctypes.byref(g), ctypes.byref(cfg), st),
+                   "dk_w4a16_gemv_rowshard")
+        for r in self.shards:
+            _check(lib.dk_shard_wait(self.peers.flags[r], target, st), "dk_shard_wait")
+        r0 = next(iter(self.shards))
+        return self.peers.view(r0, which, (B, self.M), torch.float16)
+
+    def _nccl(self, x: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        from . import gemv
+
+        if self.peers.emulated:
+            raise RuntimeError("the NCCL exchange needs one process per rank")
+        p, s, _ = self.shards[self.peers.rank]
+        y_r = gemv(p, s, x)
+        world = self.peers.world
+        if world == 1:
+            return y_r
+        if self.M % world:
+            raise RuntimeError("the NCCL exchange needs M divisible by the world size")
+        out = torch.empty((world,) + tuple(y_r.shape), dtype=y_r.dtype, device=y_r.device)
+        dist.all_gather_into_tensor(out, y_r.contiguous(), group=self.group)
+        return out.permute(1, 0, 2).reshape(x.shape[0], self.M)
+
+
+class KParallelW4A16:
+    """y[B, M] = x[B, K] . W^T with W's reduction split over the ranks.
+
+    Each local rank keeps its group-aligned K slice as contiguous tensors on
+    the current GPU; every rank returns the same fp16 y = fp16(sum over ranks,
+    in rank order, of the fp32 partials).
+    """
+
+    def __init__(self, packed: torch.Tensor, scales: torch.Tensor, peers: PeerBuffers,
+                 max_batch: int = 1, exchange: str = "fused", group=None):
+        if exchange not in ("fused", "nccl"):
+            raise ValueError(exchange)
+        self.M, self.K = packed.shape[0], packed.shape[1] * 8
+        self.peers, self.exchange, self.group = peers, exchange, group
+        self.max_batch = int(max_batch)
+        if 4 * peers.world * self.max_batch * self.M > peers.nbytes:
+            raise ValueError("peer buffers too small for [world, max_batch, M] fp32")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.shards = {}
+        for r in peers.local_ranks():
+            p, s, k0 = slice_k(packed, scales, peers.world, r)
+            self.shards[r] = (p.to(dev), s.to(dev), k0)
+        self.out = {r: torch.empty((self.max_batch, self.M), dtype=torch.float16, device=dev)
+                    for r in self.shards}
+
+    def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        B = x.shape[0]
+        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
+            raise RuntimeError("x must be contiguous fp16 [B, K]")
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
+        if self.exchange == "nccl":
+            return self._nccl(x)
+        lib, st, cfg = self.peers.lib, _stream(), _cfg(pdl)
+        which, target = self.peers.begin()
+        for r, (p, s, k0) in self.shards.items():
+            g = self.peers.group(r, which)
+            _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), x.data_ptr() + 2 * k0,
+                                            self.K, self.M, p.shape[1] * 8, B, ctypes.byref(g),
+                                            ctypes.byref(cfg), st),
+                   "dk_w4a16_gemv_kshard")
+        for r in self.shards:
+            y = self.out[r][:B]
+            _check(lib.dk_shard_reduce(self.peers.bufs[which][r], self.peers.world, self.M, B,
+                                       y.data_ptr(), self.peers.flags[r], target, st),
+                   "dk_shard_reduce")
+        return self.out[next(iter(self.shards))][:B]
+
+    def _nccl(self, x: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        if self.peers.emulated:
+            raise RuntimeError("the NCCL exchange needs one process per rank")
+        p, s, k0 = self.shards[self.peers.rank]
+        B = x.shape[0]
+        kn = p.shape[1] * 8
+        xs = x[:, k0:k0 + kn].contiguous()
+        y32 = torch.empty((B, self.M), dtype=torch.float32, device=x.device)
+        cfg = capi.default_config(version=5, flags=capi.DK_FLAG_F32_OUT)
+        _check(capi.gemv(p.data_ptr(), s.data_ptr(), xs.data_ptr(), y32.data_ptr(), self.M, kn,
+                         B, cfg, 0, 0, _stream()), "dk_w4a16_gemv")
+        if self.peers.world > 1:
+            dist.all_reduce(y32, group=self.group)
+        return y32.half()

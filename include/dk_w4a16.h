@@ -77,6 +77,11 @@ typedef enum dk_kernel_version {
                           * Only valid when the previous kernel on the stream
                           * does not write `packed` or `scales`. */
 
+#define DK_FLAG_F32_OUT 0x2u /* version 5 (and the reuse path) only: y is fp32
+                              * [B, M] -- pass the float pointer as `y` -- with
+                              * no rounding to fp16.  Other versions return
+                              * DK_ERR_UNSUPPORTED. */
+
 /* gemv_w4a16.h:22-27 GemvLaunchConfig, same fields and defaults, plus flags. */
 typedef struct dk_gemv_config {
   int version;       /* 0..5, default 5 */
@@ -124,6 +129,69 @@ DK_API dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales, co
 DK_API dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint16_t* scales,
                                               const uint16_t* x, uint16_t* y, int M, int K, int B,
                                               int split_k, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Sharded GEMV across the GPUs of one node (one process per GPU).  No
+ * counterpart in the reference, which is single-GPU; these serve the
+ * row-parallel (output rows split, results all-gathered) and K-parallel
+ * (reduction split, partials summed) layouts, with the exchange fused into
+ * the GEMV: the kernel stores its results straight into every rank's buffer
+ * over NVLink peer memory and then counts itself in on every rank's arrival
+ * counter.  A rank may read the gathered result once its counter reaches
+ * world * (number of sharded calls made so far on this group).
+ * ------------------------------------------------------------------------ */
+#define DK_MAX_SHARDS 8
+typedef struct dk_shard_group {
+  int rank;                        /* this process's rank, 0..world-1 */
+  int world;                       /* number of ranks, 1..DK_MAX_SHARDS */
+  void* bufs[DK_MAX_SHARDS];       /* every rank's result buffer, mapped here */
+  unsigned* flags[DK_MAX_SHARDS];  /* every rank's arrival counter, mapped here */
+  unsigned* done;                  /* this rank's own finished-CTA counter
+                                    * (device memory, zero before the first
+                                    * call; the kernel leaves it at zero) */
+} dk_shard_group;
+
+/* Row-parallel shard: this rank holds rows [row0, row0 + M_shard) of an
+ * [M_total, K] weight (packed [M_shard, K/8], scales [M_shard, K/128]); x is
+ * the full fp16 [B, K].  Every rank's bufs[g] is fp16 [B, M_total]; this call
+ * writes columns [row0, row0 + M_shard) of all of them.  B <= 32, version 5
+ * (cfg->version must be 5; DK_FLAG_PDL is honoured). */
+DK_API dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_t* scales,
+                                        const uint16_t* x, int M_shard, int row0, int M_total,
+                                        int K, int B, const dk_shard_group* group,
+                                        const dk_gemv_config* cfg, void* stream);
+
+/* K-parallel shard: this rank holds a group-aligned K slice of an [M, K]
+ * weight as its own contiguous packed [M, K_shard/8] and scales
+ * [M, K_shard/128]; x points at the slice's first column of the full fp16 x,
+ * whose rows are ldx elements apart.  Every rank's bufs[g] is fp32
+ * [world][B][M]; this call writes slot `rank` of all of them.  B <= 32. */
+DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* scales,
+                                      const uint16_t* x, int ldx, int M, int K_shard, int B,
+                                      const dk_shard_group* group, const dk_gemv_config* cfg,
+                                      void* stream);
+
+/* Enqueue a wait until *flag >= target (unsigned, wrap-safe) on `stream`:
+ * later work on the stream sees what the counted ranks wrote.  Bounded: after
+ * about 2 s it records the timeout in dk_device_error and lets the stream go
+ * on. */
+DK_API dk_status dk_shard_wait(const unsigned* flag, unsigned target, void* stream);
+
+/* K-parallel finish: wait as dk_shard_wait, then y[b, m] = fp16(sum over
+ * r = 0..world-1, in that order, of partials[r][b][m]).  Every rank computes
+ * the same bits. */
+DK_API dk_status dk_shard_reduce(const float* partials, int world, int M, int B, uint16_t* y,
+                                 const unsigned* flag, unsigned target, void* stream);
+
+/* Peer memory for the buffers and counters above: a plain device allocation
+ * on the current device (zero-filled), its inter-process handle, and the
+ * mapping of another process's handle into this one (CUDA IPC over NVLink). */
+#define DK_PEER_HANDLE_BYTES 64
+DK_API dk_status dk_peer_alloc(size_t bytes, void** ptr);
+DK_API dk_status dk_peer_free(void* ptr);
+DK_API dk_status dk_peer_export(const void* ptr, unsigned char* handle);
+DK_API dk_status dk_peer_import(const unsigned char* handle, void** ptr);
+DK_API dk_status dk_peer_close(void* ptr);
 
 /* STREAM-style HBM probes (gemv_w4a16.h:39-43).  `bytes` must be a multiple
  * of 16 and the pointers 16-byte aligned.  dk_stream_read writes one float

@@ -1,0 +1,184 @@
+"""Host side of the sharded path (decode_kernel.sharded), on CPU.
+
+The partitioning arithmetic -- which rows / which whole 128-wide groups of K
+each rank owns -- and the exchange it implies are checked with gloo process
+groups (world 2 and 3, spawned ranks on 127.0.0.1): every rank computes its
+shard with the CPU oracle, the ranks all-gather (row-parallel) or all-reduce
+(K-parallel) through torch.distributed, and the result must equal the oracle
+on the whole matrix.  The CUDA kernels are exercised by test_sharded_gpu.py.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from dkhelpers import make_problem
+
+
+def test_row_range_covers_every_row_once():
+    from decode_kernel.sharded import row_range
+
+    for M in (1, 7, 64, 4096, 11008, 28672):
+        for world in range(1, 9):
+            seen = []
+            for r in range(world):
+                row0, rows = row_range(M, world, r)
+                assert rows >= M // world and rows <= M // world + 1
+                seen.extend(range(row0, row0 + rows))
+            assert seen == list(range(M))
+
+
+def test_k_range_is_group_aligned_and_covers_k():
+    from decode_kernel.sharded import k_range
+
+    for K in (128, 4096, 11008, 28672):
+        for world in range(1, 9):
+            cols = []
+            for r in range(world):
+                k0, kn = k_range(K, world, r)
+                assert k0 % 128 == 0 and kn % 128 == 0
+                cols.extend(range(k0, k0 + kn))
+            assert cols == list(range(K))
+    with pytest.raises(ValueError):
+        k_range(200, 2, 0)
+    with pytest.raises(ValueError):
+        k_range(256, 2, 2)
+
+
+def test_slices_are_the_owned_parts():
+    import torch
+
+    from decode_kernel.sharded import slice_k, slice_rows
+
+    packed, scales, _ = make_problem(40, 1024, 1, seed=3)
+    tp = torch.from_numpy(packed)
+    ts = torch.from_numpy(scales.view(np.int16)).view(torch.float16)
+    rows = [slice_rows(tp, ts, 3, r) for r in range(3)]
+    assert torch.equal(torch.cat([p for p, _, _ in rows]), tp)
+    assert [r0 for _, _, r0 in rows] == [0, 13, 26]
+    ks = [slice_k(tp, ts, 3, r) for r in range(3)]
+    assert torch.equal(torch.cat([p for p, _, _ in ks], dim=1), tp)
+    assert torch.equal(torch.cat([s for _, s, _ in ks], dim=1), ts)
+    assert all(p.is_contiguous() and s.is_contiguous() for p, s, _ in ks)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, layout: str, M: int, K: int, B: int,
+               out_path: str) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from decode_kernel.sharded import k_range, row_range
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        packed, scales, x = make_problem(M, K, B, seed=91)
+        if layout == "row":
+            row0, rows = row_range(M, world, rank)
+            part = O.linear_fp32(x, packed[row0:row0 + rows], scales[row0:row0 + rows])
+            pieces = [None] * world
+            dist.all_gather_object(pieces, part)
+            y = np.concatenate(pieces, axis=1)
+        else:
+            k0, kn = k_range(K, world, rank)
+            p = np.ascontiguousarray(packed[:, k0 // 8:(k0 + kn) // 8])
+            s = np.ascontiguousarray(scales[:, k0 // 128:(k0 + kn) // 128])
+            part = torch.from_numpy(O.linear_fp32(np.ascontiguousarray(x[:, k0:k0 + kn]), p, s))
+            dist.all_reduce(part)
+            y = part.numpy()
+        np.save(f"{out_path}.{rank}.npy", y)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("layout", ["row", "k"])
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_exchange_matches_whole_matrix(layout, world, tmp_path):
+    import torch.multiprocessing as mp
+
+    from oracle import oracle as O
+
+    M, K, B = 96, 1408, 2  # 11 groups: K slices of unequal size at world 2 and 3
+    out = str(tmp_path / "y")
+    mp.start_processes(_rank_main, args=(world, _free_port(), layout, M, K, B, out),
+                       nprocs=world, start_method="spawn", join=True)
+    packed, scales, x = make_problem(M, K, B, seed=91)
+    ref = O.linear_fp32(x, packed, scales)
+    for r in range(world):
+        y = np.load(f"{out}.{r}.npy")
+        assert y.shape == ref.shape
+        if layout == "row":
+            assert np.array_equal(y, ref)  # row slices are independent
+        else:
+            assert np.abs(y - ref).max() < 1e-4
+
+
+def _group(world=2, rank=0, **kw):
+    from decode_kernel import capi
+
+    g = capi.ShardGroup()
+    g.rank, g.world = rank, world
+    for r in range(min(world, capi.DK_MAX_SHARDS)):
+        g.bufs[r] = 4096 * (r + 1)
+        g.flags[r] = 8192 * (r + 1)
+    g.done = 64
+    for k, v in kw.items():
+        setattr(g, k, v)
+    return g
+
+
+def test_shard_entries_reject_bad_arguments_without_a_device():
+    import ctypes
+
+    from decode_kernel import capi
+
+    lib = capi.load()
+    cfg = capi.default_config()
+
+    def row(g, M_shard=64, row0=0, M_total=128, K=256, B=1, c=cfg):
+        return lib.dk_w4a16_gemv_rowshard(16, 16, 16, M_shard, row0, M_total, K, B,
+                                          ctypes.byref(g), ctypes.byref(c), None)
+
+    assert row(_group(world=0)) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(world=9)) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(world=2, rank=2)) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(done=None)) == capi.DK_ERR_INVALID_ARG
+    bad = _group()
+    bad.bufs[1] = None
+    assert row(bad) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(), row0=100) == capi.DK_ERR_INVALID_ARG  # rows past M_total
+    assert row(_group(), K=200) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(), B=33) == capi.DK_ERR_UNSUPPORTED
+    assert row(_group(), c=capi.default_config(version=3)) == capi.DK_ERR_UNSUPPORTED
+    assert row(_group(), c=capi.default_config(flags=capi.DK_FLAG_F32_OUT)) == \
+        capi.DK_ERR_UNSUPPORTED
+    # K-parallel: x rows must be at least K_shard apart and 16-byte aligned.
+    assert lib.dk_w4a16_gemv_kshard(16, 16, 16, 128, 64, 256, 1, ctypes.byref(_group()),
+                                    ctypes.byref(cfg), None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_w4a16_gemv_kshard(16, 16, 16, 260, 64, 256, 1, ctypes.byref(_group()),
+                                    ctypes.byref(cfg), None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_wait(None, 1, None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(16, 0, 8, 1, 16, 16, 1, None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(16, 9, 8, 1, 16, 16, 1, None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(16, 2, 0, 1, 16, 16, 1, None) == capi.DK_OK  # empty
+
+
+def test_f32_flag_only_on_the_streaming_kernel():
+    from decode_kernel import capi
+
+    for v in range(5):
+        c = capi.default_config(version=v, flags=capi.DK_FLAG_F32_OUT)
+        assert capi.gemv(16, 16, 16, 16, 64, 256, 1, c) == capi.DK_ERR_UNSUPPORTED
+    assert capi.gemv(16, 16, 16, 16, 64, 256, 1,
+                     capi.default_config(flags=0x4)) == capi.DK_ERR_INVALID_ARG

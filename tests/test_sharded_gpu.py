@@ -1,0 +1,197 @@
+"""The sharded GEMV on the GPU: fused exchange over peer memory.
+
+Single GPU: ``PeerBuffers(emulate=G)`` keeps all G ranks' buffers and
+counters on one GPU and launches every rank's kernel in turn on one stream,
+so the fused path -- each rank's epilogue storing into every rank's buffer,
+the arrival counters, the bounded waits, the rank-ordered K reduction -- runs
+for G up to 8 without G GPUs.  Row-parallel results must equal the unsharded
+GEMV bit for bit (row slices are independent); K-parallel results must equal,
+bit for bit, fp16 of the rank-ordered sum of the fp32 slice GEMVs, and be
+within 1e-2 of the oracle.  With two or more GPUs the same layers run as real
+ranks (spawned processes, NCCL for the handle exchange).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from dkhelpers import MAX_ABS, capi_gemv, make_problem, max_err, oracle_y, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def f32_gemv(tp, ts, tx):
+    from decode_kernel import capi
+
+    M, K, B = tp.shape[0], tp.shape[1] * 8, tx.shape[0]
+    y = torch.full((B, M), float("nan"), dtype=torch.float32, device=tp.device)
+    capi.check(capi.gemv(tp.data_ptr(), ts.data_ptr(), tx.data_ptr(), y.data_ptr(), M, K, B,
+                         capi.default_config(flags=capi.DK_FLAG_F32_OUT), 0, 0,
+                         torch.cuda.current_stream().cuda_stream), "f32 gemv")
+    return y
+
+
+@pytest.mark.parametrize("B", [1, 5, 9, 33])
+@pytest.mark.parametrize("reuse", [0, 1])
+def test_f32_output_rounds_to_the_fp16_output(B, reuse, cuda_device):
+    from decode_kernel import capi
+
+    packed, scales, x = make_problem(300, 2048, B, seed=60 + B)
+    tp, ts, tx = to_device(packed, scales, x)
+    y16 = capi_gemv(tp, ts, tx, capi.default_config(reuse_weights=reuse))
+    M, K = 300, 2048
+    y32 = torch.full((B, M), float("nan"), dtype=torch.float32, device=cuda_device)
+    cfg = capi.default_config(reuse_weights=reuse, flags=capi.DK_FLAG_F32_OUT)
+    capi.check(capi.gemv(tp.data_ptr(), ts.data_ptr(), tx.data_ptr(), y32.data_ptr(), M, K, B,
+                         cfg, 0, 0, 0), "f32")
+    torch.cuda.synchronize()
+    assert torch.equal(y32.half(), y16)
+    assert max_err(y32, oracle_y(x, packed, scales)) < MAX_ABS
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("B", [1, 3])
+def test_row_parallel_emulated_is_the_unsharded_gemv(world, B, cuda_device):
+    from decode_kernel.sharded import PeerBuffers, RowParallelW4A16
+
+    M, K = 1376, 4096
+    packed, scales, x = make_problem(M, K, B, seed=200 + world)
+    tp, ts, tx = to_device(packed, scales, x)
+    peers = PeerBuffers(2 * B * M, emulate=world)
+    layer = RowParallelW4A16(tp, ts, peers, max_batch=B)
+    try:
+        for call in range(3):  # both buffer sets, counters accumulating
+            xc = (tx * (1 + call)).contiguous()
+            full = capi_gemv(tp, ts, xc)
+            layer(xc, pdl=(call == 1))
+            torch.cuda.synchronize()
+            which = call & 1
+            for r in range(world):
+                assert torch.equal(peers.view(r, which, (B, M), torch.float16), full), (call, r)
+        from decode_kernel import capi
+
+        assert capi.load().dk_device_error(-1, 1) == 0
+    finally:
+        peers.close()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("B", [1, 4])
+def test_k_parallel_emulated_sums_the_slices_in_rank_order(world, B, cuda_device):
+    from decode_kernel.sharded import KParallelW4A16, PeerBuffers, slice_k
+
+    M, K = 512, 11008  # 86 groups: unequal slices for 4 and 8 ranks
+    packed, scales, x = make_problem(M, K, B, seed=300 + world, std=0.05)
+    tp, ts, tx = to_device(packed, scales, x)
+    peers = PeerBuffers(4 * world * B * M, emulate=world)
+    layer = KParallelW4A16(tp, ts, peers, max_batch=B)
+    try:
+        for call in range(2):
+            y = layer(tx).clone()
+            outs = [layer.out[r][:B].clone() for r in range(world)]
+            torch.cuda.synchronize()
+            for o in outs[1:]:
+                assert torch.equal(o, outs[0])
+            # fp16(sum in rank order of the fp32 slice GEMVs), bit for bit.
+            acc = torch.zeros((B, M), dtype=torch.float32, device=cuda_device)
+            for r in range(world):
+                p, s, k0 = slice_k(tp, ts, world, r)
+                acc += f32_gemv(p, s, tx[:, k0:k0 + p.shape[1] * 8].contiguous())
+            assert torch.equal(y, acc.half())
+            assert max_err(y, oracle_y(x, packed, scales)) < MAX_ABS
+    finally:
+        peers.close()
+
+
+def test_shard_wait_on_a_counter_nobody_bumps_times_out(cuda_device):
+    # The bounded wait gives up after ~2 s, records the timeout in the
+    # device error word and lets the stream continue; the context stays usable.
+    from decode_kernel import capi
+
+    lib = capi.load()
+    lib.dk_device_error(-1, 1)
+    flag = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    capi.check(lib.dk_shard_wait(flag.data_ptr(), 1, torch.cuda.current_stream().cuda_stream),
+               "dk_shard_wait")
+    torch.cuda.synchronize()
+    assert lib.dk_device_error(-1, 1) == 1
+    assert lib.dk_device_error(-1, 0) == 0
+    # and a wait whose target is already met returns at once
+    flag.fill_(5)
+    capi.check(lib.dk_shard_wait(flag.data_ptr(), 5, 0), "dk_shard_wait")
+    torch.cuda.synchronize()
+    assert lib.dk_device_error(-1, 0) == 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from decode_kernel.sharded import KParallelW4A16, PeerBuffers, RowParallelW4A16
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        M, K, B = 2048, 4096, 2
+        packed, scales, x = make_problem(M, K, B, seed=77)
+        dev = torch.device("cuda", rank)
+        tp = torch.from_numpy(packed).to(dev)
+        ts = torch.from_numpy(scales.view(np.int16)).to(dev).view(torch.float16)
+        tx = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.float16)
+        peers = PeerBuffers(4 * world * B * M)
+        rowl = RowParallelW4A16(tp, ts, peers, max_batch=B)
+        kl = KParallelW4A16(tp, ts, peers, max_batch=B)
+        y_row = rowl(tx).clone()
+        y_k = kl(tx).clone()
+        y_row_nccl = RowParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
+        y_k_nccl = KParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
+        torch.cuda.synchronize()
+        from decode_kernel import capi
+
+        err = capi.load().dk_device_error(-1, 0)
+        np.savez(f"{out_path}.{rank}.npz", row=y_row.float().cpu().numpy(),
+                 k=y_k.float().cpu().numpy(), row_nccl=y_row_nccl.float().cpu().numpy(),
+                 k_nccl=y_k_nccl.float().cpu().numpy(), err=err)
+        dist.barrier()
+        peers.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_two_real_ranks_fused_and_nccl(tmp_path):
+    import torch.multiprocessing as mp
+
+    world = 2
+    out = str(tmp_path / "y")
+    env = dict(os.environ)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world,
+                           start_method="spawn", join=True)
+    finally:
+        os.environ.clear()
+        os.environ.update(env)
+    packed, scales, x = make_problem(2048, 4096, 2, seed=77)
+    ref = oracle_y(x, packed, scales)
+    got = [np.load(f"{out}.{r}.npz") for r in range(world)]
+    for g in got:
+        assert int(g["err"]) == 0
+        assert np.array_equal(g["row"], got[0]["row"]) and np.array_equal(g["k"], got[0]["k"])
+        assert np.array_equal(g["row"], g["row_nccl"])  # same kernel rows, gathered
+        for key in ("row", "k", "row_nccl", "k_nccl"):
+            assert np.abs(g[key] - ref).max() < MAX_ABS, key
