@@ -464,6 +464,127 @@ def run_ours(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# Sharded model shapes (row- / K-parallel across the ranks, strong scaling)
+# --------------------------------------------------------------------------
+
+def model_gemvs(workload: str, layers: int):
+    """(M, K, layout) of every GEMV in one decode step of the model shapes:
+    Llama-2-7B (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008; all
+    row-parallel -- 86 groups of K in down do not divide by 4 or 8) and
+    Llama-70B-shaped layers (q/o 8192x8192 and gate/up 28672x8192
+    row-parallel, down 8192x28672 K-parallel)."""
+    if workload == "llama7b":
+        one = [(4096, 4096, "row")] * 4 + [(11008, 4096, "row")] * 2 + [(4096, 11008, "row")]
+    else:
+        one = [(8192, 8192, "row"), (8192, 8192, "row"), (28672, 8192, "row"),
+               (28672, 8192, "row"), (8192, 28672, "k")]
+    return one * layers
+
+
+def run_sharded(args) -> None:
+    import datetime
+
+    import torch
+
+    from decode_kernel.quantize import quantize_and_pack_cuda
+    from decode_kernel.sharded import (KParallelW4A16, PeerBuffers, RowParallelW4A16, k_range,
+                                       row_range)
+
+    ws, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B = args.batch
+    layers = args.layers or (32 if args.workload == "llama7b" else 8)
+    shapes = model_gemvs(args.workload, layers)
+    maxm = max(m for m, _, _ in shapes)
+    peers = PeerBuffers(max(2 * B * maxm, 4 * ws * B * maxm))
+    xs = {}
+    mods, shard_bytes = [], 0
+    for i, (M, K, layout) in enumerate(shapes):
+        g = torch.Generator(device=dev).manual_seed(7000 + i)  # same weights on every rank
+        w = torch.randn(M, K, generator=g, device=dev) * 0.02
+        p, s = quantize_and_pack_cuda(w)
+        del w
+        cls = RowParallelW4A16 if layout == "row" else KParallelW4A16
+        mods.append(cls(p, s, peers, max_batch=B, exchange=args.exchange))
+        del p, s
+        if K not in xs:
+            gx = torch.Generator(device=dev).manual_seed(K)
+            xs[K] = torch.randn(B, K, generator=gx, device=dev).half()
+        if layout == "row":
+            _, rows = row_range(M, ws, rank)
+            shard_bytes += gemv_bytes(rows, K, B) + B * (M - rows) * 2
+        else:
+            _, kn = k_range(K, ws, rank)
+            shard_bytes += gemv_bytes(M, kn, B) + B * M * 2 * (ws - 1)
+    torch.cuda.synchronize()
+    pdl = not args.no_pdl and args.exchange == "fused"
+    # this library's kernels per step: GEMV + wait (+ the K-parallel sum)
+    launches = sum((2 if lay == "row" else 3) if args.exchange == "fused" else 1
+                   for _, _, lay in shapes)
+
+    def step():
+        for mod, (M, K, _) in zip(mods, shapes):
+            mod(xs[K], pdl=pdl)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms, float(shard_bytes)], dtype=torch.float64, device=dev)
+    total = torch.tensor([float(shard_bytes)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(total)
+    from decode_kernel import capi
+
+    err = capi.load().dk_device_error(-1, 0)
+    del graph
+    torch.cuda.synchronize()
+    peers.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_max = float(t[0].item())
+    value = float(total.item()) * args.steps / (ms_max / 1e3) / 1e9
+    line = {
+        "metric": f"aggregate HBM read GB/s, {args.workload} decode-step GEMV stack",
+        "value": value, "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "us_per_token": ms_max * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4*f16->f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} x{layers} layers, {len(shapes)} GEMVs, B={B}",
+                   "global_batch": B, "exchange": args.exchange, "pdl": pdl,
+                   "parallelism": f"row/K-parallel x{ws}",
+                   "l2": "inputs larger than L2 (the step streams every layer's weights)"},
+        "device_error": err, "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -478,11 +599,18 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["gemv", "llama7b", "llama70b"], default="gemv",
+                    help="gemv: the BASELINE metric; llama7b / llama70b: the sharded model "
+                         "decode-step GEMV stacks (strong scaling over the ranks)")
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--layers", type=int, default=0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "gemv":
+        run_sharded(args)
     else:
         run_ours(args)
 

@@ -65,6 +65,8 @@ struct OutSpec {
   void* dst[kMaxShards] = {};
   unsigned* flags[kMaxShards] = {};  // shard modes: each rank's arrival counter
   unsigned* done = nullptr;          // shard modes: this rank's finished-CTA counter
+  unsigned* expect = nullptr;        // shard modes: arrivals this rank has waited for
+  int await_all = 0;                 // the last CTA waits for every rank's part
 };
 
 struct GemvParams {
@@ -104,7 +106,11 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
 
 // Shard modes: once every CTA of this rank has stored its rows, count this
 // rank in on every rank's arrival counter (each call adds 1 per rank, so a
-// rank waits for world * calls).  Called by the one warp that wrote y.
+// rank waits for world * calls).  With await_all the CTA that counted the
+// rank in then waits (bounded) until every rank's part has arrived here, so
+// the kernel -- and the stream -- completes only with the gather complete,
+// while a PDL-launched successor already streams its weights.  Called by the
+// one warp that wrote y.
 __device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
   if (p.out.mode < kOutRowShard) return;
   __threadfence_system();  // this lane's stores to every rank, before the count
@@ -115,6 +121,22 @@ __device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
       *p.out.done = 0;  // the next call on this stream starts from zero
       __threadfence_system();
       for (int g = 0; g < p.out.world; ++g) atomicAdd_system(p.out.flags[g], 1u);
+      if (p.out.await_all) {
+        const unsigned target = *p.out.expect + (unsigned)p.out.world;
+        const unsigned* flag = p.out.flags[p.out.rank];
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+          unsigned v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+          if ((int)(v - target) >= 0) break;
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicExch(&g_dk_device_error, kDevWaitTimeout);
+            break;
+          }
+          __nanosleep(64);
+        }
+        *p.out.expect = target;
+      }
     }
   }
 }
@@ -1244,7 +1266,7 @@ static dk_status validate_config(const dk_gemv_config& c) {
   if (c.split_k < 1 || c.split_k > 32) return DK_ERR_INVALID_ARG;
   if (c.warps_per_row < 1 || c.warps_per_row > 8) return DK_ERR_INVALID_ARG;
   if (c.warps_per_row > 1 && (c.version != 1 || c.reuse_weights)) return DK_ERR_INVALID_ARG;
-  if (c.flags & ~(DK_FLAG_PDL | DK_FLAG_F32_OUT)) return DK_ERR_INVALID_ARG;
+  if (c.flags & ~(DK_FLAG_PDL | DK_FLAG_F32_OUT | DK_FLAG_SHARD_WAIT)) return DK_ERR_INVALID_ARG;
   return DK_OK;
 }
 
@@ -1279,6 +1301,7 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
   if (!y) return DK_ERR_INVALID_ARG;
   const bool f32 = (c.flags & DK_FLAG_F32_OUT) != 0;
   if (f32 && !f32_supported(c)) return DK_ERR_UNSUPPORTED;
+  if (c.flags & DK_FLAG_SHARD_WAIT) return DK_ERR_INVALID_ARG;  // sharded calls only
   if (K == 0) {  // empty reduction: y = 0
     const size_t elem = f32 ? sizeof(float) : sizeof(uint16_t);
     const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)B * M * elem, st);
@@ -1377,8 +1400,9 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   dk_status s = validate_config(c);
   if (s != DK_OK) return s;
   if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
+  const bool await_all = (c.flags & DK_FLAG_SHARD_WAIT) != 0;
   if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
-      !g->done)
+      !g->done || (await_all && !g->expect))
     return DK_ERR_INVALID_ARG;
   for (int i = 0; i < g->world; ++i)
     if (!g->bufs[i] || !g->flags[i]) return DK_ERR_INVALID_ARG;
@@ -1394,6 +1418,8 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
     p.out.flags[i] = g->flags[i];
   }
   p.out.done = g->done;
+  p.out.expect = g->expect;
+  p.out.await_all = await_all ? 1 : 0;
   p.ws = nullptr;
   p.counters = nullptr;
   p.y = nullptr;

@@ -1,6 +1,8 @@
 // dk_shard.cu -- the exchange side of the sharded GEMV: bounded arrival waits,
 // the K-parallel partial reduction, and the peer-memory plumbing (CUDA IPC
-// handles, mapped with lazy peer access over NVLink).
+// handles, mapped with lazy peer access over NVLink).  The waits keep their
+// position in the count on the device (dk_shard_group::expect), so a captured
+// CUDA graph of sharded calls replays correctly.
 //
 // The GEMV kernels themselves (dk_w4a16_gemv_rowshard / _kshard in
 // dk_gemv.cu) store their results into every rank's buffer and then add one
@@ -37,18 +39,19 @@ __device__ bool wait_count(const unsigned* flag, unsigned target, int* err) {
   }
 }
 
-__global__ void k_shard_wait(const unsigned* flag, unsigned target, int* err) {
-  if (threadIdx.x == 0) wait_count(flag, target, err);
+// One more call's arrivals: wait for *flag >= *expect + world, then advance
+// *expect (single thread).
+__global__ void k_shard_wait(const unsigned* flag, unsigned* expect, unsigned world, int* err) {
+  if (threadIdx.x == 0) {
+    const unsigned target = *expect + world;
+    wait_count(flag, target, err);
+    *expect = target;
+  }
 }
 
 // y[i] = fp16(sum_r part[r][i]) in ascending r; part is [world][n].  The
 // partials were stored by other GPUs: read them from L2.
-__global__ void k_shard_reduce(const float* part, int world, int n, __half* y,
-                               const unsigned* flag, unsigned target, int* err) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) ok = wait_count(flag, target, err) ? 1 : 0;
-  __syncthreads();
-  if (!ok) return;
+__global__ void k_shard_sum(const float* part, int world, int n, __half* y) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int r = 0; r < world; ++r) s = __fadd_rn(s, __ldcg(part + (size_t)r * n + i));
@@ -61,28 +64,34 @@ __global__ void k_shard_reduce(const float* part, int world, int n, __half* y,
 
 using namespace dk;
 
-extern "C" dk_status dk_shard_wait(const unsigned* flag, unsigned target, void* stream) {
-  if (!flag) return DK_ERR_INVALID_ARG;
+static bool group_ok(const dk_shard_group* g) {
+  return g && g->world >= 1 && g->world <= DK_MAX_SHARDS && g->rank >= 0 &&
+         g->rank < g->world && g->flags[g->rank] && g->expect;
+}
+
+extern "C" dk_status dk_shard_wait(const dk_shard_group* group, void* stream) {
+  if (!group_ok(group)) return DK_ERR_INVALID_ARG;
   int* err = device_error_address();
   if (!err) return DK_ERR_CUDA;
-  k_shard_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, target, err);
+  k_shard_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      group->flags[group->rank], group->expect, (unsigned)group->world, err);
   return check_launch("k_shard_wait");
 }
 
-extern "C" dk_status dk_shard_reduce(const float* partials, int world, int M, int B, uint16_t* y,
-                                     const unsigned* flag, unsigned target, void* stream) {
-  if (!partials || !y || !flag || world < 1 || world > DK_MAX_SHARDS || M < 0 || B < 0)
+extern "C" dk_status dk_shard_reduce(const dk_shard_group* group, int M, int B, uint16_t* y,
+                                     int waited, void* stream) {
+  if (!group_ok(group) || !group->bufs[group->rank] || !y || M < 0 || B < 0)
     return DK_ERR_INVALID_ARG;
   const long long n = (long long)M * B;
-  if (n == 0) return DK_OK;
   if (n > (1ll << 30)) return DK_ERR_UNSUPPORTED;
-  int* err = device_error_address();
-  if (!err) return DK_ERR_CUDA;
+  dk_status s = waited ? DK_OK : dk_shard_wait(group, stream);
+  if (s != DK_OK || n == 0) return s;
   const int threads = 256;
   const int blocks = (int)std::min<long long>((n + threads - 1) / threads, 4ll * sm_count(-1));
-  k_shard_reduce<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      partials, world, (int)n, reinterpret_cast<__half*>(y), flag, target, err);
-  return check_launch("k_shard_reduce");
+  k_shard_sum<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(group->bufs[group->rank]), group->world, (int)n,
+      reinterpret_cast<__half*>(y));
+  return check_launch("k_shard_sum");
 }
 
 extern "C" dk_status dk_peer_alloc(size_t bytes, void** ptr) {

@@ -22,6 +22,7 @@ DK_ERR_WORKSPACE = 6
 
 DK_FLAG_PDL = 0x1
 DK_FLAG_F32_OUT = 0x2
+DK_FLAG_SHARD_WAIT = 0x4
 DK_QUANT_TORCH_CUDA_SCALE = 0x1
 DK_NOALLOC_SCRATCH_BYTES = 8 << 20
 DK_MAX_SHARDS = 8
@@ -43,7 +44,7 @@ class GemvConfig(ctypes.Structure):
 class ShardGroup(ctypes.Structure):
     """struct dk_shard_group: this rank, the world size, every rank's result
     buffer and arrival counter as mapped in this process, and this rank's own
-    finished-CTA counter."""
+    finished-CTA and already-waited-for counters."""
 
     _fields_ = [
         ("rank", ctypes.c_int),
@@ -51,6 +52,7 @@ class ShardGroup(ctypes.Structure):
         ("bufs", ctypes.c_void_p * DK_MAX_SHARDS),
         ("flags", ctypes.c_void_p * DK_MAX_SHARDS),
         ("done", ctypes.c_void_p),
+        ("expect", ctypes.c_void_p),
     ]
 
 
@@ -65,8 +67,8 @@ SIGNATURES = {
                                     ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_kshard": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
                                   ctypes.POINTER(GemvConfig), _P]),
-    "dk_shard_wait": (_I, [_P, _U, _P]),
-    "dk_shard_reduce": (_I, [_P, _I, _I, _I, _P, _P, _U, _P]),
+    "dk_shard_wait": (_I, [ctypes.POINTER(ShardGroup), _P]),
+    "dk_shard_reduce": (_I, [ctypes.POINTER(ShardGroup), _I, _I, _P, _I, _P]),
     "dk_peer_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
     "dk_peer_free": (_I, [_P]),
     "dk_peer_export": (_I, [_P, ctypes.c_char_p]),

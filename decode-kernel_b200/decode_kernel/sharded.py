@@ -13,8 +13,12 @@ Two layouts (the reference is single-GPU; these serve its 7B-stack and
 ``exchange="fused"`` (default) runs the exchange inside the GEMV: the kernel's
 epilogue stores its results straight into every rank's buffer over NVLink peer
 memory and counts the rank in on every rank's arrival counter
-(``dk_w4a16_gemv_rowshard`` / ``dk_w4a16_gemv_kshard``); a bounded wait
-(``dk_shard_wait`` / ``dk_shard_reduce``) then releases the stream.
+(``dk_w4a16_gemv_rowshard`` / ``dk_w4a16_gemv_kshard``).  Ranks on their own
+GPUs run with ``DK_FLAG_SHARD_WAIT``: the kernel's last CTA waits (bounded)
+for every rank's part, so the call completes with the gather complete while a
+PDL-launched successor already streams its weights; emulated ranks wait with a
+separate ``dk_shard_wait`` after all of them have run.  One rank alone skips
+the exchange and runs the plain GEMV.
 ``exchange="nccl"`` runs the plain GEMV followed by torch.distributed
 collectives -- the baseline the fused path is measured against.
 
@@ -126,6 +130,7 @@ class PeerBuffers:
             self.bufs = [[self._alloc(self.nbytes) for _ in range(self.world)] for _ in range(2)]
             self.flags = [self._alloc(16) for _ in range(self.world)]
             self.dones = [self._alloc(16) for _ in range(self.world)]
+            self.expects = [self._alloc(16) for _ in range(self.world)]
             return
         import torch.distributed as dist
 
@@ -136,6 +141,7 @@ class PeerBuffers:
             raise ValueError(f"world {self.world} outside 1..{capi.DK_MAX_SHARDS}")
         mine = [self._alloc(self.nbytes), self._alloc(self.nbytes), self._alloc(16)]
         self.dones = [self._alloc(16)]
+        self.expects = [self._alloc(16)]
         if self.world == 1:
             self.bufs = [[mine[0]], [mine[1]]]
             self.flags = [mine[2]]
@@ -180,6 +186,7 @@ class PeerBuffers:
             g.bufs[r] = self.bufs[which][r]
             g.flags[r] = self.flags[r]
         g.done = self.dones[rank if self.emulated else 0]
+        g.expect = self.expects[rank if self.emulated else 0]
         return g
 
     def view(self, rank: int, which: int, shape: Sequence[int], dtype: torch.dtype) -> torch.Tensor:
@@ -193,11 +200,11 @@ class PeerBuffers:
         return torch.as_tensor(_DeviceArray(self.bufs[which][rank], shape, typestr),
                                device=torch.device("cuda", torch.cuda.current_device()))
 
-    def begin(self) -> tuple[int, int]:
-        """Next call: (buffer set to write, arrival target to wait for)."""
+    def begin(self) -> int:
+        """Buffer set the next call writes (the sets alternate)."""
         which = self.calls & 1
         self.calls += 1
-        return which, (self.calls * self.world) & 0xFFFFFFFF
+        return which
 
     def close(self) -> None:
         torch.cuda.synchronize()
@@ -219,8 +226,9 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _cfg(pdl: bool) -> capi.GemvConfig:
-    return capi.default_config(version=5, flags=capi.DK_FLAG_PDL if pdl else 0)
+def _cfg(pdl: bool, await_all: bool = False) -> capi.GemvConfig:
+    flags = (capi.DK_FLAG_PDL if pdl else 0) | (capi.DK_FLAG_SHARD_WAIT if await_all else 0)
+    return capi.default_config(version=5, flags=flags)
 
 
 # --------------------------------------------------------------------------
@@ -248,7 +256,8 @@ class RowParallelW4A16:
         self.shards = {}
         for r in peers.local_ranks():
             p, s, row0 = slice_rows(packed, scales, peers.world, r)
-            self.shards[r] = (p.to(dev).contiguous(), s.to(dev).contiguous(), row0)
+            # own copies, so the caller's full tensors can be freed
+            self.shards[r] = (p.to(dev).clone(), s.to(dev).clone(), row0)
 
     def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
         if x.dim() == 1:
@@ -260,18 +269,29 @@ class RowParallelW4A16:
             raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         if self.exchange == "nccl":
             return self._nccl(x)
-        lib, st, cfg = self.peers.lib, _stream(), _cfg(pdl)
-        which, target = self.peers.begin()
+        lib, st = self.peers.lib, _stream()
+        which = self.peers.begin()
+        r0 = next(iter(self.shards))
+        y = self.peers.view(r0, which, (B, self.M), torch.float16)
+        if self.peers.world == 1 and not self.peers.emulated:  # nothing to exchange
+            p, s, _ = self.shards[r0]
+            _check(capi.gemv(p.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(), self.M,
+                             self.K, B, _cfg(pdl), 0, 0, st), "dk_w4a16_gemv")
+            return y
+        # Ranks on their own GPUs wait inside the kernel; emulated ranks
+        # sharing this GPU's stream wait after all of them have run.
+        inline = not self.peers.emulated
+        cfg = _cfg(pdl, await_all=inline)
+        groups = {r: self.peers.group(r, which) for r in self.shards}
         for r, (p, s, row0) in self.shards.items():
-            g = self.peers.group(r, which)
             _check(lib.dk_w4a16_gemv_rowshard(p.data_ptr(), s.data_ptr(), x.data_ptr(),
                                               p.shape[0], row0, self.M, self.K, B,
-                                              ctypes.byref(g), ctypes.byref(cfg), st),
+                                              ctypes.byref(groups[r]), ctypes.byref(cfg), st),
                    "dk_w4a16_gemv_rowshard")
-        for r in self.shards:
-            _check(lib.dk_shard_wait(self.peers.flags[r], target, st), "dk_shard_wait")
-        r0 = next(iter(self.shards))
-        return self.peers.view(r0, which, (B, self.M), torch.float16)
+        if not inline:
+            for r in self.shards:
+                _check(lib.dk_shard_wait(ctypes.byref(groups[r]), st), "dk_shard_wait")
+        return y
 
     def _nccl(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
@@ -327,20 +347,27 @@ class KParallelW4A16:
             raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         if self.exchange == "nccl":
             return self._nccl(x)
-        lib, st, cfg = self.peers.lib, _stream(), _cfg(pdl)
-        which, target = self.peers.begin()
+        lib, st = self.peers.lib, _stream()
+        r0 = next(iter(self.shards))
+        if self.peers.world == 1 and not self.peers.emulated:  # nothing to exchange
+            p, s, _ = self.shards[r0]
+            _check(capi.gemv(p.data_ptr(), s.data_ptr(), x.data_ptr(), self.out[r0].data_ptr(),
+                             self.M, self.K, B, _cfg(pdl), 0, 0, st), "dk_w4a16_gemv")
+            return self.out[r0][:B]
+        inline = not self.peers.emulated
+        cfg = _cfg(pdl, await_all=inline)
+        which = self.peers.begin()
+        groups = {r: self.peers.group(r, which) for r in self.shards}
         for r, (p, s, k0) in self.shards.items():
-            g = self.peers.group(r, which)
             _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), x.data_ptr() + 2 * k0,
-                                            self.K, self.M, p.shape[1] * 8, B, ctypes.byref(g),
-                                            ctypes.byref(cfg), st),
+                                            self.K, self.M, p.shape[1] * 8, B,
+                                            ctypes.byref(groups[r]), ctypes.byref(cfg), st),
                    "dk_w4a16_gemv_kshard")
         for r in self.shards:
-            y = self.out[r][:B]
-            _check(lib.dk_shard_reduce(self.peers.bufs[which][r], self.peers.world, self.M, B,
-                                       y.data_ptr(), self.peers.flags[r], target, st),
+            _check(lib.dk_shard_reduce(ctypes.byref(groups[r]), self.M, B,
+                                       self.out[r][:B].data_ptr(), int(inline), st),
                    "dk_shard_reduce")
-        return self.out[next(iter(self.shards))][:B]
+        return self.out[r0][:B]
 
     def _nccl(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist

@@ -82,6 +82,15 @@ typedef enum dk_kernel_version {
                               * no rounding to fp16.  Other versions return
                               * DK_ERR_UNSUPPORTED. */
 
+#define DK_FLAG_SHARD_WAIT 0x4u /* sharded calls only: the call completes on the
+                                 * stream only once every rank's part has
+                                 * arrived here (the last CTA waits, bounded,
+                                 * and advances group->expect), so no
+                                 * dk_shard_wait is needed.  Only for ranks on
+                                 * different GPUs running concurrently: ranks
+                                 * that share one GPU and one stream must use
+                                 * dk_shard_wait instead. */
+
 /* gemv_w4a16.h:22-27 GemvLaunchConfig, same fields and defaults, plus flags. */
 typedef struct dk_gemv_config {
   int version;       /* 0..5, default 5 */
@@ -149,6 +158,10 @@ typedef struct dk_shard_group {
   unsigned* done;                  /* this rank's own finished-CTA counter
                                     * (device memory, zero before the first
                                     * call; the kernel leaves it at zero) */
+  unsigned* expect;                /* this rank's count of arrivals already
+                                    * waited for (device memory, zero before
+                                    * the first call; advanced by the waits
+                                    * below, so captured graphs replay) */
 } dk_shard_group;
 
 /* Row-parallel shard: this rank holds rows [row0, row0 + M_shard) of an
@@ -171,17 +184,20 @@ DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* sca
                                       const dk_shard_group* group, const dk_gemv_config* cfg,
                                       void* stream);
 
-/* Enqueue a wait until *flag >= target (unsigned, wrap-safe) on `stream`:
- * later work on the stream sees what the counted ranks wrote.  Bounded: after
- * about 2 s it records the timeout in dk_device_error and lets the stream go
- * on. */
-DK_API dk_status dk_shard_wait(const unsigned* flag, unsigned target, void* stream);
+/* Enqueue the wait for the sharded call just made on this group: until this
+ * rank's counter (flags[rank]) reaches *expect + world, then *expect +=
+ * world.  Later work on the stream sees what every rank stored.  Bounded:
+ * after about 2 s it records the timeout in dk_device_error and lets the
+ * stream go on. */
+DK_API dk_status dk_shard_wait(const dk_shard_group* group, void* stream);
 
-/* K-parallel finish: wait as dk_shard_wait, then y[b, m] = fp16(sum over
- * r = 0..world-1, in that order, of partials[r][b][m]).  Every rank computes
- * the same bits. */
-DK_API dk_status dk_shard_reduce(const float* partials, int world, int M, int B, uint16_t* y,
-                                 const unsigned* flag, unsigned target, void* stream);
+/* K-parallel finish: the wait above (skipped when `waited` is non-zero, i.e.
+ * the GEMV ran with DK_FLAG_SHARD_WAIT), then y[b, m] = fp16(sum over
+ * r = 0..world-1, in that order, of partials[r][b][m]) with partials = this
+ * rank's buffer bufs[rank] (fp32 [world][B][M]).  Every rank computes the
+ * same bits. */
+DK_API dk_status dk_shard_reduce(const dk_shard_group* group, int M, int B, uint16_t* y,
+                                 int waited, void* stream);
 
 /* Peer memory for the buffers and counters above: a plain device allocation
  * on the current device (zero-filled), its inter-process handle, and the

@@ -168,10 +168,19 @@ def test_shard_entries_reject_bad_arguments_without_a_device():
                                     ctypes.byref(cfg), None) == capi.DK_ERR_INVALID_ARG
     assert lib.dk_w4a16_gemv_kshard(16, 16, 16, 260, 64, 256, 1, ctypes.byref(_group()),
                                     ctypes.byref(cfg), None) == capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_wait(None, 1, None) == capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_reduce(16, 0, 8, 1, 16, 16, 1, None) == capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_reduce(16, 9, 8, 1, 16, 16, 1, None) == capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_reduce(16, 2, 0, 1, 16, 16, 1, None) == capi.DK_OK  # empty
+    assert lib.dk_shard_wait(None, None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_wait(ctypes.byref(_group()), None) == capi.DK_ERR_INVALID_ARG  # no expect
+    assert lib.dk_shard_wait(ctypes.byref(_group(world=9, expect=16)), None) == \
+        capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(ctypes.byref(_group(world=0, expect=16)), 8, 1, 16, 0, None) == \
+        capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(ctypes.byref(_group(expect=16)), 8, 1, None, 0, None) == \
+        capi.DK_ERR_INVALID_ARG
+    # the in-kernel wait needs the group's expect counter, and sharded calls
+    assert row(_group(), c=capi.default_config(flags=capi.DK_FLAG_SHARD_WAIT)) == \
+        capi.DK_ERR_INVALID_ARG
+    assert capi.gemv(16, 16, 16, 16, 64, 256, 1,
+                     capi.default_config(flags=capi.DK_FLAG_SHARD_WAIT)) == capi.DK_ERR_INVALID_ARG
 
 
 def test_f32_flag_only_on_the_streaming_kernel():
@@ -181,4 +190,4 @@ def test_f32_flag_only_on_the_streaming_kernel():
         c = capi.default_config(version=v, flags=capi.DK_FLAG_F32_OUT)
         assert capi.gemv(16, 16, 16, 16, 64, 256, 1, c) == capi.DK_ERR_UNSUPPORTED
     assert capi.gemv(16, 16, 16, 16, 64, 256, 1,
-                     capi.default_config(flags=0x4)) == capi.DK_ERR_INVALID_ARG
+                     capi.default_config(flags=0x8)) == capi.DK_ERR_INVALID_ARG

@@ -111,21 +111,65 @@ def test_k_parallel_emulated_sums_the_slices_in_rank_order(world, B, cuda_device
 def test_shard_wait_on_a_counter_nobody_bumps_times_out(cuda_device):
     # The bounded wait gives up after ~2 s, records the timeout in the
     # device error word and lets the stream continue; the context stays usable.
+    import ctypes
+
     from decode_kernel import capi
 
     lib = capi.load()
     lib.dk_device_error(-1, 1)
-    flag = torch.zeros(4, dtype=torch.int32, device=cuda_device)
-    capi.check(lib.dk_shard_wait(flag.data_ptr(), 1, torch.cuda.current_stream().cuda_stream),
-               "dk_shard_wait")
+    counters = torch.zeros(8, dtype=torch.int32, device=cuda_device)  # flag, done, expect
+    g = capi.ShardGroup()
+    g.rank, g.world = 0, 2
+    g.bufs[0] = g.bufs[1] = counters.data_ptr()
+    g.flags[0] = g.flags[1] = counters.data_ptr()
+    g.done = counters.data_ptr() + 4
+    g.expect = counters.data_ptr() + 8
+    st = torch.cuda.current_stream().cuda_stream
+    capi.check(lib.dk_shard_wait(ctypes.byref(g), st), "dk_shard_wait")
     torch.cuda.synchronize()
     assert lib.dk_device_error(-1, 1) == 1
     assert lib.dk_device_error(-1, 0) == 0
-    # and a wait whose target is already met returns at once
-    flag.fill_(5)
-    capi.check(lib.dk_shard_wait(flag.data_ptr(), 5, 0), "dk_shard_wait")
+    assert int(counters[2]) == 2  # the count moved on by one call (world 2)
+    # A wait whose arrivals are all in returns at once and advances the count.
+    counters[0] = 4
+    capi.check(lib.dk_shard_wait(ctypes.byref(g), st), "dk_shard_wait")
     torch.cuda.synchronize()
     assert lib.dk_device_error(-1, 0) == 0
+    assert int(counters[2]) == 4
+
+
+def test_row_parallel_step_replays_from_a_cuda_graph(cuda_device):
+    # The waits keep their place in the arrival count on the device, so a
+    # captured step replays: every replay waits for that replay's arrivals.
+    from decode_kernel import capi
+    from decode_kernel.sharded import PeerBuffers, RowParallelW4A16
+
+    M, K, B, world = 1024, 2048, 1, 4
+    packed, scales, x = make_problem(M, K, B, seed=5)
+    tp, ts, tx = to_device(packed, scales, x)
+    peers = PeerBuffers(2 * B * M, emulate=world)
+    layer = RowParallelW4A16(tp, ts, peers, max_batch=B)
+    try:
+        xin = tx.clone()
+        layer(xin)
+        layer(xin)  # warm-up outside capture, both buffer sets
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer(xin)
+            layer(xin)
+        for step in range(3):
+            xin.copy_(tx * (step + 2))
+            full = capi_gemv(tp, ts, xin)
+            g.replay()
+            torch.cuda.synchronize()
+            for which in (0, 1):
+                for r in range(world):
+                    assert torch.equal(peers.view(r, which, (B, M), torch.float16), full)
+        assert capi.load().dk_device_error(-1, 1) == 0
+        del g
+    finally:
+        peers.close()
 
 
 def _free_port() -> int:
