@@ -239,6 +239,42 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Every wait in this library is bounded: 2 s of wall clock.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Sharded calls: a release store of `epoch` into another GPU's (or this
+// GPU's) arrival slot, and the warp-wide wait until slots[r * stride + b] >=
+// epoch (wrap-safe) for every r < world, b < grid.  The wait reads with
+// acquire semantics at system scope; on timeout it records kDevWaitTimeout in
+// *err and returns false.  Call the wait with all 32 lanes.
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ inline bool wait_slots(const unsigned* slots, int stride, int world, int grid,
+                                  unsigned epoch, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int n = world * grid;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    bool mine = true;
+    for (int i = lane; i < n; i += 32) {
+      const int r = i / grid, b = i - r * grid;
+      if ((int)(ld_acquire_sys_u32(slots + r * stride + b) - epoch) < 0) {
+        mine = false;
+        break;
+      }
+    }
+    if (__all_sync(0xffffffffu, mine)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (lane == 0) atomicExch(err, 1);
+      return false;
+    }
+    __nanosleep(32);
+  }
+}
+
 #ifdef DK_DEVICE_GLOBALS
 // A wait that runs out records kDevWaitTimeout in g_dk_device_error, raises
 // the CTA's abort flag (so every other wait in the CTA returns at once) and

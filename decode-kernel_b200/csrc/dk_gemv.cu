@@ -63,10 +63,10 @@ struct OutSpec {
   int world = 1, rank = 0;
   int ld = 0, col0 = 0;
   void* dst[kMaxShards] = {};
-  unsigned* flags[kMaxShards] = {};  // shard modes: each rank's arrival counter
-  unsigned* done = nullptr;          // shard modes: this rank's finished-CTA counter
-  unsigned* expect = nullptr;        // shard modes: arrivals this rank has waited for
-  int await_all = 0;                 // the last CTA waits for every rank's part
+  unsigned* slots[kMaxShards] = {};  // shard modes: each rank's arrival slots
+  unsigned* seq = nullptr;           // shard modes: this rank's [calls done, grid]
+  int grid = 0;                      // shard modes: CTAs per rank (same on every rank)
+  int await_all = 0;                 // CTA 0 waits for every rank's part
 };
 
 struct GemvParams {
@@ -104,41 +104,27 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
   }
 }
 
-// Shard modes: once every CTA of this rank has stored its rows, count this
-// rank in on every rank's arrival counter (each call adds 1 per rank, so a
-// rank waits for world * calls).  With await_all the CTA that counted the
-// rank in then waits (bounded) until every rank's part has arrived here, so
-// the kernel -- and the stream -- completes only with the gather complete,
-// while a PDL-launched successor already streams its weights.  Called by the
-// one warp that wrote y.
+// Shard modes: after this CTA's last store of y, mark its arrival slot in
+// every rank's slot array with the call's sequence number (release stores at
+// system scope: the warp's stores to that rank are visible before the mark).
+// With await_all CTA 0 then waits (bounded) until every slot of this rank's
+// own array carries the number, so the kernel -- and the stream -- completes
+// with the gather complete while a PDL-launched successor already streams
+// its weights.  Called by the one warp that wrote y, all lanes.
 __device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
   if (p.out.mode < kOutRowShard) return;
-  __threadfence_system();  // this lane's stores to every rank, before the count
+  pdl_wait();  // seq was advanced by the previous sharded call
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(p.out.seq) + 1;
   __syncwarp();
-  if (lane == 0) {
-    const unsigned old = atomicAdd(p.out.done, 1u);
-    if (old == gridDim.x - 1) {
-      *p.out.done = 0;  // the next call on this stream starts from zero
-      __threadfence_system();
-      for (int g = 0; g < p.out.world; ++g) atomicAdd_system(p.out.flags[g], 1u);
-      if (p.out.await_all) {
-        const unsigned target = *p.out.expect + (unsigned)p.out.world;
-        const unsigned* flag = p.out.flags[p.out.rank];
-        const uint64_t t0 = globaltimer_ns();
-        for (;;) {
-          unsigned v;
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-          if ((int)(v - target) >= 0) break;
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicExch(&g_dk_device_error, kDevWaitTimeout);
-            break;
-          }
-          __nanosleep(64);
-        }
-        *p.out.expect = target;
-      }
-    }
+  if (lane < p.out.world)
+    st_release_sys(p.out.slots[lane] + p.out.rank * DK_SHARD_SLOTS + blockIdx.x, epoch);
+  if (blockIdx.x != 0) return;
+  if (p.out.await_all) {
+    wait_slots(p.out.slots[p.out.rank], DK_SHARD_SLOTS, p.out.world, (int)gridDim.x, epoch,
+               &g_dk_device_error);
+    if (lane == 0) p.out.seq[0] = epoch;
   }
+  if (lane == 0) p.out.seq[1] = gridDim.x;
 }
 
 // ---------------------------------------------------------------------------
@@ -1148,7 +1134,8 @@ dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t 
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
-  const int grid = std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
+  const int grid =
+      p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
   return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW>, dim3(grid), dim3(NCW * 32 + 32),
                 smem, st, pdl, tmap, p);
 }
@@ -1392,6 +1379,10 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
 // Sharded GEMV (row-parallel and K-parallel): the v5 pipeline with its
 // epilogue storing into every rank's buffer and counting the rank in.
 // ---------------------------------------------------------------------------
+// CTAs of a sharded call: one per SM, or one per 8 rows of `rows` if fewer;
+// every rank derives it from the same numbers, so every rank has the same.
+static int shard_grid(int rows) { return std::max(1, std::min(sm_count(-1), (rows + 7) / 8)); }
+
 static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_gemv_config* cfg,
                               cudaStream_t st) {
   dk_gemv_config c;
@@ -1401,11 +1392,12 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   if (s != DK_OK) return s;
   if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
   const bool await_all = (c.flags & DK_FLAG_SHARD_WAIT) != 0;
+  if (sm_count(-1) > DK_SHARD_SLOTS) return DK_ERR_UNSUPPORTED;
   if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
-      !g->done || (await_all && !g->expect))
+      !g->seq)
     return DK_ERR_INVALID_ARG;
   for (int i = 0; i < g->world; ++i)
-    if (!g->bufs[i] || !g->flags[i]) return DK_ERR_INVALID_ARG;
+    if (!g->bufs[i] || !g->slots[i]) return DK_ERR_INVALID_ARG;
   if (p.M <= 0 || p.K <= 0 || p.K % DK_GROUP_SIZE != 0 || p.B <= 0) return DK_ERR_INVALID_ARG;
   if (p.B > kMaxBatchPerPass) return DK_ERR_UNSUPPORTED;
   if (!p.packed || !p.scales || !p.x || !aligned16(p.packed) || !aligned16(p.x) ||
@@ -1415,10 +1407,9 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   p.out.rank = g->rank;
   for (int i = 0; i < g->world; ++i) {
     p.out.dst[i] = g->bufs[i];
-    p.out.flags[i] = g->flags[i];
+    p.out.slots[i] = g->slots[i];
   }
-  p.out.done = g->done;
-  p.out.expect = g->expect;
+  p.out.seq = g->seq;
   p.out.await_all = await_all ? 1 : 0;
   p.ws = nullptr;
   p.counters = nullptr;
@@ -1445,6 +1436,8 @@ extern "C" dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_
   p.out.mode = kOutRowShard;
   p.out.ld = M_total;
   p.out.col0 = row0;
+  if (group && group->world >= 1)  // the same on every rank: from the largest shard
+    p.out.grid = shard_grid((M_total + group->world - 1) / group->world);
   return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
 }
 
@@ -1462,6 +1455,7 @@ extern "C" dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t*
   p.B = B;
   p.out.mode = kOutKShard;
   p.out.ld = M;
+  p.out.grid = shard_grid(M);
   return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
 }
 

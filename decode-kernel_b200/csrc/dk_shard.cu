@@ -1,15 +1,15 @@
 // dk_shard.cu -- the exchange side of the sharded GEMV: bounded arrival waits,
 // the K-parallel partial reduction, and the peer-memory plumbing (CUDA IPC
-// handles, mapped with lazy peer access over NVLink).  The waits keep their
-// position in the count on the device (dk_shard_group::expect), so a captured
-// CUDA graph of sharded calls replays correctly.
+// handles, mapped with lazy peer access over NVLink).  The call sequence
+// number lives on the device (dk_shard_group::seq), so a captured CUDA graph
+// of sharded calls replays correctly.
 //
 // The GEMV kernels themselves (dk_w4a16_gemv_rowshard / _kshard in
-// dk_gemv.cu) store their results into every rank's buffer and then add one
-// to every rank's arrival counter per call, after a system-scope fence.  The
-// waits here read the local counter with acquire semantics at system scope,
-// so everything the counted ranks stored before their fence is visible to the
-// work that follows on the stream.
+// dk_gemv.cu) store their results into every rank's buffer and then, per CTA,
+// release-store the call's sequence number into that CTA's slot of every
+// rank's slot array.  The waits read the local slots with acquire semantics
+// at system scope, so everything the ranks stored before marking their slots
+// is visible to the work that follows on the stream.
 #include <cstring>
 
 #include "dk_device.cuh"
@@ -18,35 +18,13 @@
 namespace dk {
 namespace {
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// True once *flag >= target (wrap-safe); false after the wait bound, with the
-// timeout recorded in the device error word.
-__device__ bool wait_count(const unsigned* flag, unsigned target, int* err) {
-  if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    __nanosleep(128);
-    if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(err, kDevWaitTimeout);
-      return false;
-    }
-  }
-}
-
-// One more call's arrivals: wait for *flag >= *expect + world, then advance
-// *expect (single thread).
-__global__ void k_shard_wait(const unsigned* flag, unsigned* expect, unsigned world, int* err) {
-  if (threadIdx.x == 0) {
-    const unsigned target = *expect + world;
-    wait_count(flag, target, err);
-    *expect = target;
-  }
+// The wait for one more call: every slot of this rank's array must carry
+// seq[0] + 1 (seq[1] = CTAs per rank of that call, stored by the GEMV).
+__global__ void k_shard_wait(const unsigned* slots, unsigned* seq, int world, int* err) {
+  const unsigned epoch = seq[0] + 1;
+  const int grid = (int)seq[1];
+  wait_slots(slots, DK_SHARD_SLOTS, world, grid, epoch, err);
+  if (threadIdx.x == 0) seq[0] = epoch;
 }
 
 // y[i] = fp16(sum_r part[r][i]) in ascending r; part is [world][n].  The
@@ -66,15 +44,15 @@ using namespace dk;
 
 static bool group_ok(const dk_shard_group* g) {
   return g && g->world >= 1 && g->world <= DK_MAX_SHARDS && g->rank >= 0 &&
-         g->rank < g->world && g->flags[g->rank] && g->expect;
+         g->rank < g->world && g->slots[g->rank] && g->seq;
 }
 
 extern "C" dk_status dk_shard_wait(const dk_shard_group* group, void* stream) {
   if (!group_ok(group)) return DK_ERR_INVALID_ARG;
   int* err = device_error_address();
   if (!err) return DK_ERR_CUDA;
-  k_shard_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      group->flags[group->rank], group->expect, (unsigned)group->world, err);
+  k_shard_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(group->slots[group->rank],
+                                                                 group->seq, group->world, err);
   return check_launch("k_shard_wait");
 }
 

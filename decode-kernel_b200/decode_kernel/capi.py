@@ -26,6 +26,7 @@ DK_FLAG_SHARD_WAIT = 0x4
 DK_QUANT_TORCH_CUDA_SCALE = 0x1
 DK_NOALLOC_SCRATCH_BYTES = 8 << 20
 DK_MAX_SHARDS = 8
+DK_SHARD_SLOTS = 256
 DK_PEER_HANDLE_BYTES = 64
 
 
@@ -43,16 +44,15 @@ class GemvConfig(ctypes.Structure):
 
 class ShardGroup(ctypes.Structure):
     """struct dk_shard_group: this rank, the world size, every rank's result
-    buffer and arrival counter as mapped in this process, and this rank's own
-    finished-CTA and already-waited-for counters."""
+    buffer and arrival-slot array as mapped in this process, and this rank's
+    own [calls completed, CTAs per rank] pair."""
 
     _fields_ = [
         ("rank", ctypes.c_int),
         ("world", ctypes.c_int),
         ("bufs", ctypes.c_void_p * DK_MAX_SHARDS),
-        ("flags", ctypes.c_void_p * DK_MAX_SHARDS),
-        ("done", ctypes.c_void_p),
-        ("expect", ctypes.c_void_p),
+        ("slots", ctypes.c_void_p * DK_MAX_SHARDS),
+        ("seq", ctypes.c_void_p),
     ]
 
 

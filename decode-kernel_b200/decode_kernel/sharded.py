@@ -12,7 +12,7 @@ Two layouts (the reference is single-GPU; these serve its 7B-stack and
 
 ``exchange="fused"`` (default) runs the exchange inside the GEMV: the kernel's
 epilogue stores its results straight into every rank's buffer over NVLink peer
-memory and counts the rank in on every rank's arrival counter
+memory and marks its arrival slot in every rank's slot array
 (``dk_w4a16_gemv_rowshard`` / ``dk_w4a16_gemv_kshard``).  Ranks on their own
 GPUs run with ``DK_FLAG_SHARD_WAIT``: the kernel's last CTA waits (bounded)
 for every rank's part, so the call completes with the gather complete while a
@@ -108,8 +108,11 @@ def _check(status: int, what: str) -> None:
     capi.check(status, what)
 
 
+_SLOT_BYTES = 4 * capi.DK_MAX_SHARDS * capi.DK_SHARD_SLOTS
+
+
 class PeerBuffers:
-    """Result buffers (two sets, used in turn) and arrival counters of every
+    """Result buffers (two sets, used in turn) and arrival slots of every
     rank, mapped in this process.
 
     ``nbytes`` is the size of one result buffer.  With a process group each
@@ -128,9 +131,8 @@ class PeerBuffers:
             if not 1 <= self.world <= capi.DK_MAX_SHARDS:
                 raise ValueError(f"world {self.world} outside 1..{capi.DK_MAX_SHARDS}")
             self.bufs = [[self._alloc(self.nbytes) for _ in range(self.world)] for _ in range(2)]
-            self.flags = [self._alloc(16) for _ in range(self.world)]
-            self.dones = [self._alloc(16) for _ in range(self.world)]
-            self.expects = [self._alloc(16) for _ in range(self.world)]
+            self.slots = [self._alloc(_SLOT_BYTES) for _ in range(self.world)]
+            self.seqs = [self._alloc(16) for _ in range(self.world)]
             return
         import torch.distributed as dist
 
@@ -139,12 +141,11 @@ class PeerBuffers:
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         if not 1 <= self.world <= capi.DK_MAX_SHARDS:
             raise ValueError(f"world {self.world} outside 1..{capi.DK_MAX_SHARDS}")
-        mine = [self._alloc(self.nbytes), self._alloc(self.nbytes), self._alloc(16)]
-        self.dones = [self._alloc(16)]
-        self.expects = [self._alloc(16)]
+        mine = [self._alloc(self.nbytes), self._alloc(self.nbytes), self._alloc(_SLOT_BYTES)]
+        self.seqs = [self._alloc(16)]
         if self.world == 1:
             self.bufs = [[mine[0]], [mine[1]]]
-            self.flags = [mine[2]]
+            self.slots = [mine[2]]
             return
         handles = []
         for ptr in mine:
@@ -167,7 +168,7 @@ class PeerBuffers:
             table.append(row)
         self.bufs = [[table[r][0] for r in range(self.world)],
                      [table[r][1] for r in range(self.world)]]
-        self.flags = [table[r][2] for r in range(self.world)]
+        self.slots = [table[r][2] for r in range(self.world)]
 
     def _alloc(self, n: int) -> int:
         p = ctypes.c_void_p()
@@ -184,9 +185,8 @@ class PeerBuffers:
         g.rank, g.world = rank, self.world
         for r in range(self.world):
             g.bufs[r] = self.bufs[which][r]
-            g.flags[r] = self.flags[r]
-        g.done = self.dones[rank if self.emulated else 0]
-        g.expect = self.expects[rank if self.emulated else 0]
+            g.slots[r] = self.slots[r]
+        g.seq = self.seqs[rank if self.emulated else 0]
         return g
 
     def view(self, rank: int, which: int, shape: Sequence[int], dtype: torch.dtype) -> torch.Tensor:

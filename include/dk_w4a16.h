@@ -84,9 +84,9 @@ typedef enum dk_kernel_version {
 
 #define DK_FLAG_SHARD_WAIT 0x4u /* sharded calls only: the call completes on the
                                  * stream only once every rank's part has
-                                 * arrived here (the last CTA waits, bounded,
-                                 * and advances group->expect), so no
-                                 * dk_shard_wait is needed.  Only for ranks on
+                                 * arrived here (CTA 0 waits, bounded, and
+                                 * advances group->seq), so no dk_shard_wait
+                                 * is needed.  Only for ranks on
                                  * different GPUs running concurrently: ranks
                                  * that share one GPU and one stream must use
                                  * dk_shard_wait instead. */
@@ -144,24 +144,27 @@ DK_API dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint1
  * counterpart in the reference, which is single-GPU; these serve the
  * row-parallel (output rows split, results all-gathered) and K-parallel
  * (reduction split, partials summed) layouts, with the exchange fused into
- * the GEMV: the kernel stores its results straight into every rank's buffer
- * over NVLink peer memory and then counts itself in on every rank's arrival
- * counter.  A rank may read the gathered result once its counter reaches
- * world * (number of sharded calls made so far on this group).
+ * the GEMV: every CTA stores its results straight into every rank's buffer
+ * over NVLink peer memory and then, with one release store per rank, marks
+ * its arrival slot in every rank's slot array with the call's sequence
+ * number.  A rank may read the gathered result once all world * grid slots
+ * of its own array carry that number.  All ranks must run on the same GPU
+ * model (the grid is derived from the shape and the SM count).
  * ------------------------------------------------------------------------ */
 #define DK_MAX_SHARDS 8
+#define DK_SHARD_SLOTS 256 /* arrival slots per rank and call, >= any grid */
 typedef struct dk_shard_group {
   int rank;                        /* this process's rank, 0..world-1 */
   int world;                       /* number of ranks, 1..DK_MAX_SHARDS */
   void* bufs[DK_MAX_SHARDS];       /* every rank's result buffer, mapped here */
-  unsigned* flags[DK_MAX_SHARDS];  /* every rank's arrival counter, mapped here */
-  unsigned* done;                  /* this rank's own finished-CTA counter
-                                    * (device memory, zero before the first
-                                    * call; the kernel leaves it at zero) */
-  unsigned* expect;                /* this rank's count of arrivals already
-                                    * waited for (device memory, zero before
-                                    * the first call; advanced by the waits
-                                    * below, so captured graphs replay) */
+  unsigned* slots[DK_MAX_SHARDS];  /* every rank's arrival slots, mapped here:
+                                    * unsigned [DK_MAX_SHARDS][DK_SHARD_SLOTS],
+                                    * zero before the first call */
+  unsigned* seq;                   /* this rank's own unsigned[2] in device
+                                    * memory, zero before the first call:
+                                    * [0] sharded calls completed on this group,
+                                    * [1] CTAs per rank of the last call.  Kept
+                                    * on the device so captured graphs replay. */
 } dk_shard_group;
 
 /* Row-parallel shard: this rank holds rows [row0, row0 + M_shard) of an
@@ -184,11 +187,10 @@ DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* sca
                                       const dk_shard_group* group, const dk_gemv_config* cfg,
                                       void* stream);
 
-/* Enqueue the wait for the sharded call just made on this group: until this
- * rank's counter (flags[rank]) reaches *expect + world, then *expect +=
- * world.  Later work on the stream sees what every rank stored.  Bounded:
- * after about 2 s it records the timeout in dk_device_error and lets the
- * stream go on. */
+/* Enqueue the wait for the sharded call just made on this group: until every
+ * arrival slot of this rank's array carries seq[0] + 1, then seq[0] += 1.
+ * Later work on the stream sees what every rank stored.  Bounded: after about
+ * 2 s it records the timeout in dk_device_error and lets the stream go on. */
 DK_API dk_status dk_shard_wait(const dk_shard_group* group, void* stream);
 
 /* K-parallel finish: the wait above (skipped when `waited` is non-zero, i.e.

@@ -131,8 +131,8 @@ def _group(world=2, rank=0, **kw):
     g.rank, g.world = rank, world
     for r in range(min(world, capi.DK_MAX_SHARDS)):
         g.bufs[r] = 4096 * (r + 1)
-        g.flags[r] = 8192 * (r + 1)
-    g.done = 64
+        g.slots[r] = 8192 * (r + 1)
+    g.seq = 64
     for k, v in kw.items():
         setattr(g, k, v)
     return g
@@ -153,7 +153,7 @@ def test_shard_entries_reject_bad_arguments_without_a_device():
     assert row(_group(world=0)) == capi.DK_ERR_INVALID_ARG
     assert row(_group(world=9)) == capi.DK_ERR_INVALID_ARG
     assert row(_group(world=2, rank=2)) == capi.DK_ERR_INVALID_ARG
-    assert row(_group(done=None)) == capi.DK_ERR_INVALID_ARG
+    assert row(_group(seq=None)) == capi.DK_ERR_INVALID_ARG
     bad = _group()
     bad.bufs[1] = None
     assert row(bad) == capi.DK_ERR_INVALID_ARG
@@ -169,16 +169,13 @@ def test_shard_entries_reject_bad_arguments_without_a_device():
     assert lib.dk_w4a16_gemv_kshard(16, 16, 16, 260, 64, 256, 1, ctypes.byref(_group()),
                                     ctypes.byref(cfg), None) == capi.DK_ERR_INVALID_ARG
     assert lib.dk_shard_wait(None, None) == capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_wait(ctypes.byref(_group()), None) == capi.DK_ERR_INVALID_ARG  # no expect
-    assert lib.dk_shard_wait(ctypes.byref(_group(world=9, expect=16)), None) == \
+    assert lib.dk_shard_wait(ctypes.byref(_group(seq=None)), None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_wait(ctypes.byref(_group(world=9)), None) == capi.DK_ERR_INVALID_ARG
+    assert lib.dk_shard_reduce(ctypes.byref(_group(world=0)), 8, 1, 16, 0, None) == \
         capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_reduce(ctypes.byref(_group(world=0, expect=16)), 8, 1, 16, 0, None) == \
+    assert lib.dk_shard_reduce(ctypes.byref(_group()), 8, 1, None, 0, None) == \
         capi.DK_ERR_INVALID_ARG
-    assert lib.dk_shard_reduce(ctypes.byref(_group(expect=16)), 8, 1, None, 0, None) == \
-        capi.DK_ERR_INVALID_ARG
-    # the in-kernel wait needs the group's expect counter, and sharded calls
-    assert row(_group(), c=capi.default_config(flags=capi.DK_FLAG_SHARD_WAIT)) == \
-        capi.DK_ERR_INVALID_ARG
+    # the in-kernel wait is for sharded calls only
     assert capi.gemv(16, 16, 16, 16, 64, 256, 1,
                      capi.default_config(flags=capi.DK_FLAG_SHARD_WAIT)) == capi.DK_ERR_INVALID_ARG
 

@@ -111,31 +111,40 @@ def test_k_parallel_emulated_sums_the_slices_in_rank_order(world, B, cuda_device
 def test_shard_wait_on_a_counter_nobody_bumps_times_out(cuda_device):
     # The bounded wait gives up after ~2 s, records the timeout in the
     # device error word and lets the stream continue; the context stays usable.
+    # (A slot array that nothing marks.)
     import ctypes
 
     from decode_kernel import capi
 
     lib = capi.load()
     lib.dk_device_error(-1, 1)
-    counters = torch.zeros(8, dtype=torch.int32, device=cuda_device)  # flag, done, expect
+    slots = torch.zeros(capi.DK_MAX_SHARDS * capi.DK_SHARD_SLOTS, dtype=torch.int32,
+                        device=cuda_device)
+    seq = torch.tensor([0, 3, 0, 0], dtype=torch.int32, device=cuda_device)  # 3 CTAs per rank
     g = capi.ShardGroup()
     g.rank, g.world = 0, 2
-    g.bufs[0] = g.bufs[1] = counters.data_ptr()
-    g.flags[0] = g.flags[1] = counters.data_ptr()
-    g.done = counters.data_ptr() + 4
-    g.expect = counters.data_ptr() + 8
+    g.bufs[0] = g.bufs[1] = slots.data_ptr()
+    g.slots[0] = g.slots[1] = slots.data_ptr()
+    g.seq = seq.data_ptr()
     st = torch.cuda.current_stream().cuda_stream
     capi.check(lib.dk_shard_wait(ctypes.byref(g), st), "dk_shard_wait")
     torch.cuda.synchronize()
     assert lib.dk_device_error(-1, 1) == 1
     assert lib.dk_device_error(-1, 0) == 0
-    assert int(counters[2]) == 2  # the count moved on by one call (world 2)
-    # A wait whose arrivals are all in returns at once and advances the count.
-    counters[0] = 4
+    assert int(seq[0]) == 1  # the sequence moved on by one call
+    # All 2 x 3 slots marked with call 2: the wait returns at once.
+    for r in range(2):
+        slots[r * capi.DK_SHARD_SLOTS:r * capi.DK_SHARD_SLOTS + 3] = 2
     capi.check(lib.dk_shard_wait(ctypes.byref(g), st), "dk_shard_wait")
     torch.cuda.synchronize()
     assert lib.dk_device_error(-1, 0) == 0
-    assert int(counters[2]) == 4
+    assert int(seq[0]) == 2
+    # One slot short of call 3: times out again.
+    slots[0:3] = 3
+    slots[capi.DK_SHARD_SLOTS:capi.DK_SHARD_SLOTS + 2] = 3
+    capi.check(lib.dk_shard_wait(ctypes.byref(g), st), "dk_shard_wait")
+    torch.cuda.synchronize()
+    assert lib.dk_device_error(-1, 1) == 1
 
 
 def test_row_parallel_step_replays_from_a_cuda_graph(cuda_device):
