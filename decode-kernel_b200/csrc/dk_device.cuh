@@ -241,15 +241,18 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // Sharded calls: a release store of `epoch` into another GPU's (or this
 // GPU's) arrival slot, and the warp-wide wait until slots[r * stride + b] >=
-// epoch (wrap-safe) for every r < world, b < grid.  The wait reads with
-// acquire semantics at system scope; on timeout it records kDevWaitTimeout in
-// *err and returns false.  Call the wait with all 32 lanes.
+// epoch (wrap-safe) for every r < world, b < grid.  The wait polls with
+// relaxed system-scope loads (independent, so they overlap) and, once every
+// slot is marked, each lane issues an acquire fence, which with the release
+// stores orders everything the marking CTAs stored before what follows.  On
+// timeout it records kDevWaitTimeout in *err and returns false.  Call the
+// wait with all 32 lanes.
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+__device__ __forceinline__ unsigned ld_relaxed_sys_u32(const unsigned* p) {
   unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ inline bool wait_slots(const unsigned* slots, int stride, int world, int grid,
@@ -261,12 +264,12 @@ __device__ inline bool wait_slots(const unsigned* slots, int stride, int world, 
     bool mine = true;
     for (int i = lane; i < n; i += 32) {
       const int r = i / grid, b = i - r * grid;
-      if ((int)(ld_acquire_sys_u32(slots + r * stride + b) - epoch) < 0) {
-        mine = false;
-        break;
-      }
+      mine &= (int)(ld_relaxed_sys_u32(slots + r * stride + b) - epoch) >= 0;
     }
-    if (__all_sync(0xffffffffu, mine)) return true;
+    if (__all_sync(0xffffffffu, mine)) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      return true;
+    }
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       if (lane == 0) atomicExch(err, 1);
       return false;
