@@ -31,7 +31,7 @@ INCLUDE = REPO / "include"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB_SOURCES = ["dk_abi.cu", "dk_gemv.cu", "dk_stream.cu", "dk_quant.cu", "dk_shard.cu"]
-COMMON_DEPS = [CSRC / "dk_device.cuh", CSRC / "dk_host.h", INCLUDE / "dk_w4a16.h"]
+COMMON_DEPS = [CSRC / "dk_device.cuh", CSRC / "dk_host.h", CSRC / "dk_batch.cuh", INCLUDE / "dk_w4a16.h"]
 LIB = PKG / "libdk_b200.so"
 
 

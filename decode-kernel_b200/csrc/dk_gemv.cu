@@ -1168,6 +1168,8 @@ dk_status launch_stream_w(const GemvParams& p, const CUtensorMap& tmap, cudaStre
   return launch_stream_cfg<NT, STAMP, XS, TMAP, 16>(p, tmap, st, pdl);
 }
 
+#include "dk_batch.cuh"
+
 template <int NT, int STAMP, bool TMAP>
 dk_status launch_stream_x(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
                           bool pdl) {
@@ -1212,6 +1214,10 @@ dk_status launch_tile_nt(const GemvParams& p, int split, cudaStream_t st, bool p
 template <int STAMP>
 dk_status launch_stream_nt(const GemvParams& p, cudaStream_t st, bool pdl) {
   if (p.B <= 8) return launch_stream<1, STAMP>(p, st, pdl);
+  {
+    const dk_status b = launch_batch<STAMP>(p, st, pdl);  // tensor cores, large W, 17..32 rows
+    if (b != DK_ERR_UNSUPPORTED) return b;
+  }
   if (p.B <= 16) return launch_stream<2, STAMP>(p, st, pdl);
   return launch_stream<4, STAMP>(p, st, pdl);
 }

@@ -1,7 +1,9 @@
 """GPU parity of every GEMV kernel, called through the C ABI (dk_w4a16_gemv),
 against the CPU oracle: max-abs < 1e-2, plus the
 bit-level properties the kernel family guarantees (one canonical reduction
-order for v2/v3/v4/v5/reuse, batch- and row-invariance)."""
+order for v2/v3/v4/v5/reuse up to 8 batch rows, batch- and row-invariance
+within each kernel; 17..32 rows on large matrices run on the tensor-core
+batch kernel)."""
 
 from __future__ import annotations
 
@@ -91,14 +93,23 @@ def test_tensor_core_family_is_bitwise_identical(cuda_device):
 
 
 def test_batch_rows_are_independent(cuda_device):
-    # y[b] must not depend on which other rows share the call (bitwise).
+    # y[b] must not depend on which other rows share the call (bitwise), for
+    # each kernel path: 1..8 rows, 9..16 rows and 17..32 rows each run on one
+    # kernel; B = 33 is a pass of 32 plus a pass of 1.
     M, K, B = 512, 4096, 33
     packed, scales, x = make_problem(M, K, B, seed=21)
     tp, ts, tx = to_device(packed, scales, x)
     full = capi_gemv(tp, ts, tx, cfg())
-    for b in (0, 7, 8, 31, 32):
-        one = capi_gemv(tp, ts, tx[b:b + 1].contiguous(), cfg())
-        assert torch.equal(one[0], full[b])
+    for b in (0, 7, 8, 31):
+        # the same row at another position among 8 others (a B = 9 call)
+        idx = [(b + 5 + i) % 32 for i in range(4)] + [b] + [(b + 11 + i) % 32 for i in range(4)]
+        part = capi_gemv(tp, ts, tx[idx].contiguous(), cfg())
+        assert torch.equal(part[4], full[b]), b
+    one = capi_gemv(tp, ts, tx[32:33].contiguous(), cfg())
+    assert torch.equal(one[0], full[32])
+    five = capi_gemv(tp, ts, tx[:5].contiguous(), cfg())
+    for b in range(5):
+        assert torch.equal(capi_gemv(tp, ts, tx[b:b + 1].contiguous(), cfg())[0], five[b])
 
 
 def test_row_slices_are_independent(cuda_device):
@@ -196,3 +207,26 @@ def test_llama70b_shapes_sampled_rows(shape, batch, cuda_device):
         assert max_err(y, ref, rows=rows) < MAX_ABS
     yr = capi_gemv(tp, ts, tx, cfg(reuse_weights=1))
     assert torch.equal(yr, y)
+
+
+@pytest.mark.parametrize("B", [9, 12, 16, 17, 24, 31, 32])
+@pytest.mark.parametrize("shape", [(16, 128), (100, 1024), (333, 2304), (4096, 4096),
+                                   (16384, 384), (20001, 1024), (40000, 256)])
+def test_batch_rows_9_to_32(B, shape, cuda_device):
+    # 9..32 rows: the mma.sync streaming kernel, or -- for B > 16 on matrices
+    # of 16384+ rows -- the tcgen05 batch kernel (row tiles N = 112 .. 256,
+    # one and several waves of CTAs, ragged M, K from one group up).
+    from decode_kernel import capi
+
+    M, K = shape
+    packed, scales, x = make_problem(M, K, B, seed=7 * B + M, std=0.05)
+    tp, ts, tx = to_device(packed, scales, x)
+    y = capi_gemv(tp, ts, tx, cfg())
+    assert capi.load().dk_last_kernel_stamp(-1) == 5
+    rows = None if M * K * B <= 64 * 1024 * 1024 else (0, min(M, 2048))
+    ref = oracle_y(x, packed, scales, rows=rows)
+    assert max_err(y, ref, rows=rows) < MAX_ABS
+    yr = capi_gemv(tp, ts, tx, cfg(reuse_weights=1))
+    assert capi.load().dk_last_kernel_stamp(-1) == 15
+    assert torch.equal(yr, y)
+    assert capi.load().dk_device_error(-1, 0) == 0
