@@ -69,12 +69,25 @@ struct OutSpec {
   int await_all = 0;                 // CTA 0 waits for every rank's part
 };
 
+// v5 row segments: several weight matrices sharing x, run as one GEMV over
+// their concatenated rows (q/k/v, gate/up).  Segment s owns the global 16-row
+// tiles [tile0, tile0 + ceil(rows / 16)); its last tile may be partial.
+constexpr int kMaxSeg = DK_MAX_SEGMENTS;
+struct Segment {
+  const uint32_t* packed;  // [rows, K/8]
+  const __half* scales;    // [rows, K/128]
+  __half* y;               // [B, rows]
+  int rows, tile0;
+};
+
 struct GemvParams {
   const uint32_t* packed;  // [M, K/8]
   const __half* scales;    // [M, K/128]
   const __half* x;         // [B, ldx]
   __half* y;               // [B, M]
   int M, K, B;
+  int nseg;                // v5: 1..kMaxSeg (1: seg[0] is packed/scales/y above)
+  Segment seg[kMaxSeg];
   int ldx;                 // row stride of x in elements (K, or more for a K slice)
   float* ws;               // v4: [K/128][B][M] fp32 per-group products
   unsigned* counters;      // v4: one arrival counter per 16-row tile
@@ -83,8 +96,20 @@ struct GemvParams {
   OutSpec out;             // v5: destination of y
 };
 
-// v5 result store for batch row b, output row m.
-__device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v) {
+// A global 16-row tile of a v5 call: its segment, first row inside the
+// segment and valid rows.
+struct TileRef {
+  int seg, row, rows;
+};
+__device__ __forceinline__ TileRef tile_ref(const GemvParams& p, int gtile) {
+  int s = 0;
+  while (s + 1 < p.nseg && gtile >= p.seg[s + 1].tile0) ++s;
+  const int row = (gtile - p.seg[s].tile0) * 16;
+  return {s, row, min(16, p.seg[s].rows - row)};
+}
+
+// v5 result store for batch row b, output row m of segment seg.
+__device__ __forceinline__ void store_y(const GemvParams& p, int b, int seg, int m, float v) {
   switch (p.out.mode) {
     case kOutFloat:
       static_cast<float*>(p.out.dst[0])[(size_t)b * p.M + m] = v;
@@ -100,7 +125,7 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
         static_cast<float*>(p.out.dst[g])[((size_t)p.out.rank * p.B + b) * p.M + m] = v;
       break;
     default:
-      p.y[(size_t)b * p.M + m] = __float2half_rn(v);
+      p.seg[seg].y[(size_t)b * p.seg[seg].rows + m] = __float2half_rn(v);
   }
 }
 
@@ -702,9 +727,14 @@ __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
   }
 }
 
+// One tensor map per segment.
+struct TmapSet {
+  CUtensorMap m[kMaxSeg];
+};
+
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
 __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
-    k_stream(const __grid_constant__ CUtensorMap tmap, GemvParams p) {
+    k_stream(const __grid_constant__ TmapSet tms, GemvParams p) {
   using namespace v5;
   using CW = Consumers<NCW>;
   constexpr int kConsumerWarps = CW::kWarps;
@@ -730,9 +760,10 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   write_stamp(STAMP);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = (int)(((long long)blockIdx.x * p.M) / gridDim.x);
-  const int r1 = (int)(((long long)(blockIdx.x + 1) * p.M) / gridDim.x);
-  const int ntiles = (r1 - r0 + 15) / 16;
+  // This CTA's global tiles [t0, t0 + ntiles) of the segments' concatenation.
+  const int ntot = p.seg[p.nseg - 1].tile0 + (p.seg[p.nseg - 1].rows + 15) / 16;
+  const int t0 = (int)(((long long)blockIdx.x * ntot) / gridDim.x);
+  const int ntiles = (int)(((long long)(blockIdx.x + 1) * ntot) / gridDim.x) - t0;
   const int groups = p.K / kGroup;
   const int nk = (groups + kChunkGroups - 1) / kChunkGroups;
   const int total = ntiles * nk;
@@ -751,7 +782,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     mbar_init(xready, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    if constexpr (TMAP) tma_prefetch_desc(&tmap);
+    if constexpr (TMAP)
+      for (int i = 0; i < p.nseg; ++i) tma_prefetch_desc(&tms.m[i]);
   }
   __syncthreads();
   // A dependent GEMV launched with PDL may now start streaming its weights.
@@ -764,7 +796,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     // consumers never wait on a reduction and a pending reduction never
     // waits on a slot.
     const uint64_t policy = policy_evict_first();
-    const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(p.packed);
     const size_t row_bytes = (size_t)p.K / 2;
     StageCursor cur;
     int issued = 0, reduced = 0;
@@ -778,13 +809,15 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         bool go = !(XS && issued == kStagesBeforeX) || warp_test_wait(xready, 0);
         if (go && issued >= stages) go = warp_test_wait(&empty[cur.slot], (cur.round - 1) & 1);
         if (go) {
-          const int trow = r0 + cur.tile * 16;
+          const TileRef tr = tile_ref(p, t0 + cur.tile);
+          const Segment& sg = p.seg[tr.seg];
+          const int trow = tr.row;
           const uint32_t dst = ring + cur.slot * kStageBytes;
           if constexpr (TMAP) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
-              tma_load_3d(dst, &tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot],
-                          policy);
+              tma_load_3d(dst, &tms.m[tr.seg], 0, trow, cur.chunk * kStripsPerChunk,
+                          &full[cur.slot], policy);
             }
             // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups)
             // per cp.async.  K % 256 == 0 here, so scale rows are 4-byte
@@ -794,18 +827,19 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
-              if (trow + r < p.M && gbase + w2 < groups)
+              if (r < tr.rows && gbase + w2 < groups)
                 cp_async4(sdst + r * kScaleRowStride + w2 * 2,
-                          p.scales + (size_t)(trow + r) * groups + gbase + w2);
+                          sg.scales + (size_t)(trow + r) * groups + gbase + w2);
             }
             cp_async_mbar_arrive(&full[cur.slot]);
           } else {
-            const int rows = min(16, r1 - trow);
+            const int rows = tr.rows;
             const uint32_t bytes =
                 (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
             if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
             __syncwarp();
             if (lane < rows) {
+              const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(sg.packed);
               bulk_g2s(dst + lane * kPadRowStride,
                        wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
                        bytes, &full[cur.slot], policy);
@@ -821,8 +855,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         // Tile `reduced`: the 16 class partials of every real row and batch
         // column, added in class order.
         const float* rt = red + (reduced % kRedBufs) * kClasses * 16 * nbp;
-        const int trow = r0 + reduced * 16;
-        const int rows = min(16, r1 - trow);
+        const TileRef tr = tile_ref(p, t0 + reduced);
+        const int trow = tr.row, rows = tr.rows;
         const int nb = min(W, p.B);
         for (int o = lane; o < rows * nb; o += 32) {
           const int r = o / nb, b = o - r * nb;
@@ -830,7 +864,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
-          store_y(p, b, trow + r, sum);
+          store_y(p, b, tr.seg, trow + r, sum);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_free[reduced % kRedBufs]);
@@ -914,21 +948,19 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   // Bulk path: scales from global memory, loaded one stage ahead.
   float sn[kGroupsPerWarp][2];
   auto load_scales = [&](const StageCursor& q) {
-    const int trow = r0 + q.tile * 16;
-    const int rows = min(16, r1 - trow);
+    const TileRef tr = tile_ref(p, t0 + q.tile);
+    const __half* sp = p.seg[tr.seg].scales + (size_t)tr.row * groups;
 #pragma unroll
     for (int j = 0; j < kGroupsPerWarp; ++j) {
       const int G = min(q.chunk * kChunkGroups + warp + j * kConsumerWarps, groups - 1);
-      sn[j][0] = ldg_half(p.scales + (size_t)(trow + min(ra, rows - 1)) * groups + G);
-      sn[j][1] = ldg_half(p.scales + (size_t)(trow + min(rb, rows - 1)) * groups + G);
+      sn[j][0] = ldg_half(sp + (size_t)min(ra, tr.rows - 1) * groups + G);
+      sn[j][1] = ldg_half(sp + (size_t)min(rb, tr.rows - 1) * groups + G);
     }
   };
   StageCursor cur;
   if (!TMAP && total > 0) load_scales(cur);
 
   for (int s = 0; s < total; ++s) {
-    const int trow = r0 + cur.tile * 16;
-    const int rows = min(16, r1 - trow);
     const int cg = min(kChunkGroups, groups - cur.chunk * kChunkGroups);
     float sc[kGroupsPerWarp][2];
     if (!TMAP) {
@@ -1122,7 +1154,7 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
 }
 
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
-dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t st, bool pdl) {
+dk_status launch_stream_cfg(GemvParams p, const TmapSet& tmap, cudaStream_t st, bool pdl) {
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
@@ -1134,8 +1166,8 @@ dk_status launch_stream_cfg(GemvParams p, const CUtensorMap& tmap, cudaStream_t 
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
-  const int grid =
-      p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
+  const int tiles = p.seg[p.nseg - 1].tile0 + (p.seg[p.nseg - 1].rows + 15) / 16;
+  const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), tiles));
   return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW>, dim3(grid), dim3(NCW * 32 + 32),
                 smem, st, pdl, tmap, p);
 }
@@ -1159,7 +1191,7 @@ bool use_coresident(const GemvParams& p) {
 }
 
 template <int NT, int STAMP, bool XS, bool TMAP>
-dk_status launch_stream_w(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
+dk_status launch_stream_w(const GemvParams& p, const TmapSet& tmap, cudaStream_t st,
                           bool pdl) {
   if constexpr (NT == 1 && XS) {
     if (use_coresident<NT, XS, TMAP>(p))
@@ -1171,7 +1203,7 @@ dk_status launch_stream_w(const GemvParams& p, const CUtensorMap& tmap, cudaStre
 #include "dk_batch.cuh"
 
 template <int NT, int STAMP, bool TMAP>
-dk_status launch_stream_x(const GemvParams& p, const CUtensorMap& tmap, cudaStream_t st,
+dk_status launch_stream_x(const GemvParams& p, const TmapSet& tmap, cudaStream_t st,
                           bool pdl) {
   if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
     return launch_stream_w<1, STAMP, true, TMAP>(p, tmap, st, pdl);
@@ -1180,9 +1212,12 @@ dk_status launch_stream_x(const GemvParams& p, const CUtensorMap& tmap, cudaStre
 
 template <int NT, int STAMP>
 dk_status launch_stream(const GemvParams& p, cudaStream_t st, bool pdl) {
-  CUtensorMap tmap;
-  if (p.K % 256 == 0 && weight_tensor_map(p.packed, p.M, p.K, &tmap))
-    return launch_stream_x<NT, STAMP, true>(p, tmap, st, pdl);
+  TmapSet tmap;
+  std::memset(&tmap, 0, sizeof(tmap));
+  bool tma = p.K % 256 == 0;
+  for (int i = 0; tma && i < p.nseg; ++i)
+    tma = weight_tensor_map(p.seg[i].packed, p.seg[i].rows, p.K, &tmap.m[i]);
+  if (tma) return launch_stream_x<NT, STAMP, true>(p, tmap, st, pdl);
   std::memset(&tmap, 0, sizeof(tmap));
   return launch_stream_x<NT, STAMP, false>(p, tmap, st, pdl);
 }
@@ -1251,6 +1286,12 @@ extern "C" void dk_gemv_config_init(dk_gemv_config* cfg) {
   cfg->reuse_weights = 0;
   cfg->warps_per_row = 1;
   cfg->flags = 0;
+}
+
+// One weight matrix: segment 0 is (packed, scales, y, M).
+static void single_segment(GemvParams& p) {
+  p.nseg = 1;
+  p.seg[0] = Segment{p.packed, p.scales, p.y, p.M, 0};
 }
 
 static dk_status validate_config(const dk_gemv_config& c) {
@@ -1346,6 +1387,7 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
     }
     p.ws = partials;
     p.counters = counters;
+    single_segment(p);
     if (c.reuse_weights) {
       s = launch_stream_nt<kStampReuse>(p, st, pdl);
     } else {
@@ -1376,6 +1418,73 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
           break;
       }
     }
+    if (s != DK_OK) return s;
+  }
+  return DK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Several weight matrices sharing x in one launch (q/k/v, gate/up): the v5
+// pipeline over the concatenation of their row tiles.
+// ---------------------------------------------------------------------------
+extern "C" dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
+                                         const uint16_t* const* scales, const int* M,
+                                         uint16_t* const* y, const uint16_t* x, int K, int B,
+                                         const dk_gemv_config* cfg, void* stream) {
+  dk_gemv_config c;
+  dk_gemv_config_init(&c);
+  if (cfg) c = *cfg;
+  dk_status s = validate_config(c);
+  if (s != DK_OK) return s;
+  if (c.flags & DK_FLAG_SHARD_WAIT) return DK_ERR_INVALID_ARG;
+  if (n < 1 || n > kMaxSeg || !packed || !scales || !M || !y || K < 0 || B < 0 ||
+      K % DK_GROUP_SIZE != 0)
+    return DK_ERR_INVALID_ARG;
+  if ((c.version != 5 && !c.reuse_weights) || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
+  long long mtot = 0;
+  for (int i = 0; i < n; ++i) {
+    if (M[i] < 1 || !packed[i] || !scales[i] || !y[i]) return DK_ERR_INVALID_ARG;
+    if (K > 0 && (!aligned16(packed[i]) || (reinterpret_cast<uintptr_t>(scales[i]) & 1u)))
+      return DK_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(y[i]) & 1u) return DK_ERR_INVALID_ARG;
+    mtot += M[i];
+  }
+  if (mtot > (1ll << 30)) return DK_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0) return DK_OK;
+  if (K == 0) {
+    for (int i = 0; i < n; ++i) {
+      const cudaError_t e = cudaMemsetAsync(y[i], 0, (size_t)B * M[i] * sizeof(uint16_t), st);
+      if (e != cudaSuccess) {
+        set_cuda_error(e, "cudaMemsetAsync");
+        return DK_ERR_CUDA;
+      }
+    }
+    return DK_OK;
+  }
+  if (!x || !aligned16(x)) return DK_ERR_INVALID_ARG;
+  const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
+  for (int b0 = 0; b0 < B; b0 += kMaxBatchPerPass) {
+    GemvParams p;
+    p.packed = reinterpret_cast<const uint32_t*>(packed[0]);
+    p.scales = reinterpret_cast<const __half*>(scales[0]);
+    p.x = reinterpret_cast<const __half*>(x) + (size_t)b0 * K;
+    p.y = reinterpret_cast<__half*>(y[0]) + (size_t)b0 * M[0];
+    p.M = (int)mtot;
+    p.K = K;
+    p.ldx = K;
+    p.B = std::min(kMaxBatchPerPass, B - b0);
+    p.ws = nullptr;
+    p.counters = nullptr;
+    p.nseg = n;
+    int tile0 = 0;
+    for (int i = 0; i < n; ++i) {
+      p.seg[i] = Segment{reinterpret_cast<const uint32_t*>(packed[i]),
+                         reinterpret_cast<const __half*>(scales[i]),
+                         reinterpret_cast<__half*>(y[i]) + (size_t)b0 * M[i], M[i], tile0};
+      tile0 += (M[i] + 15) / 16;
+    }
+    s = c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl) : launch_stream_nt<5>(p, st, pdl);
     if (s != DK_OK) return s;
   }
   return DK_OK;
@@ -1420,6 +1529,7 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   p.ws = nullptr;
   p.counters = nullptr;
   p.y = nullptr;
+  single_segment(p);
   const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
   return c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl)
                          : launch_stream_nt<5>(p, st, pdl);

@@ -20,7 +20,9 @@ from .quantize import GROUP_SIZE, dequantize, quantize_and_pack, quantize_and_pa
 
 __all__ = [
     "GROUP_SIZE",
+    "W4A16Linear",
     "cuda_available",
+    "gemv_multi",
     "dequantize",
     "gemv",
     "gemv_out",
@@ -92,6 +94,42 @@ def gemv_out(
     return y
 
 
+def gemv_multi(weights, x: torch.Tensor, pdl: bool = False, reuse_weights: bool = False):
+    """Several matrices that share ``x`` (q/k/v, gate/up) in one launch.
+
+    ``weights``: up to 4 ``(packed, scales)`` pairs with the same K.  Returns
+    one fp16 [B, M_i] tensor per pair, each bit-identical to ``gemv`` of that
+    pair (the streaming kernel runs over the concatenated row tiles).
+    """
+    from . import capi
+
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if not weights or len(weights) > capi.DK_MAX_SEGMENTS:
+        raise RuntimeError(f"gemv_multi takes 1..{capi.DK_MAX_SEGMENTS} weight pairs")
+    K = x.shape[1]
+    if x.dtype != torch.float16 or not x.is_cuda or not x.is_contiguous():
+        raise RuntimeError("x must be a contiguous CUDA fp16 tensor")
+    for p, s in weights:
+        if p.dtype != torch.int32 or s.dtype != torch.float16 or not (p.is_cuda and s.is_cuda):
+            raise RuntimeError("packed must be CUDA int32 and scales CUDA fp16")
+        if p.shape[1] * 8 != K or s.shape != (p.shape[0], K // GROUP_SIZE):
+            raise RuntimeError("every matrix must be [M, K/8] with scales [M, K/128] for x's K")
+        if not (p.is_contiguous() and s.is_contiguous()):
+            raise RuntimeError("packed and scales must be contiguous")
+    ys = [torch.empty((x.shape[0], p.shape[0]), dtype=torch.float16, device=x.device)
+          for p, _ in weights]
+    flags = capi.DK_FLAG_PDL if pdl else 0
+    cfg = capi.default_config(reuse_weights=int(bool(reuse_weights)), flags=flags)
+    capi.check(capi.gemv_multi([p.data_ptr() for p, _ in weights],
+                               [s.data_ptr() for _, s in weights],
+                               [p.shape[0] for p, _ in weights], [y.data_ptr() for y in ys],
+                               x.data_ptr(), K, x.shape[0], cfg,
+                               torch.cuda.current_stream(x.device).cuda_stream),
+               "dk_w4a16_gemv_multi")
+    return ys
+
+
 def w4a16_linear(
     x: torch.Tensor,
     packed: torch.Tensor,
@@ -114,3 +152,6 @@ def w4a16_linear(
         reuse_weights=reuse_weights,
         warps_per_row=1,
     )
+
+
+from .ops import W4A16Linear  # noqa: E402  (registers torch.ops.decode_kernel.w4a16_linear)

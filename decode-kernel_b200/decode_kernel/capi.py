@@ -26,6 +26,7 @@ DK_FLAG_SHARD_WAIT = 0x4
 DK_QUANT_TORCH_CUDA_SCALE = 0x1
 DK_NOALLOC_SCRATCH_BYTES = 8 << 20
 DK_MAX_SHARDS = 8
+DK_MAX_SEGMENTS = 4
 DK_SHARD_SLOTS = 256
 DK_PEER_HANDLE_BYTES = 64
 
@@ -63,6 +64,8 @@ SIGNATURES = {
     "dk_w4a16_workspace_bytes": (_SZ, [_I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "dk_w4a16_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, _SZ, _P]),
     "dk_w4a16_gemv_splitk_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "dk_w4a16_gemv_multi": (_I, [_I, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_I),
+                                 ctypes.POINTER(_P), _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_rowshard": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
                                     ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_kshard": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
@@ -142,3 +145,16 @@ def gemv(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, M: int, K: in
 def workspace_bytes(M: int, K: int, B: int, cfg: GemvConfig | None = None) -> int:
     return int(load().dk_w4a16_workspace_bytes(M, K, B,
                                                ctypes.byref(cfg) if cfg is not None else None))
+
+
+def gemv_multi(packed_ptrs, scales_ptrs, Ms, y_ptrs, x_ptr: int, K: int, B: int,
+               cfg: GemvConfig | None = None, stream: int = 0) -> int:
+    """dk_w4a16_gemv_multi over lists of device addresses; returns the status."""
+    n = len(packed_ptrs)
+    P = (ctypes.c_void_p * n)(*packed_ptrs)
+    S = (ctypes.c_void_p * n)(*scales_ptrs)
+    Mv = (ctypes.c_int * n)(*Ms)
+    Y = (ctypes.c_void_p * n)(*y_ptrs)
+    return load().dk_w4a16_gemv_multi(n, P, S, Mv, Y, x_ptr, K, B,
+                                      ctypes.byref(cfg) if cfg is not None else None,
+                                      stream or None)

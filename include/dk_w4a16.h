@@ -139,6 +139,20 @@ DK_API dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint1
                                               const uint16_t* x, uint16_t* y, int M, int K, int B,
                                               int split_k, void* stream);
 
+/* Several weight matrices that share x -- q/k/v, gate/up -- in one launch:
+ * y[i] = x . dequant(W_i)^T for i < n (n <= DK_MAX_SEGMENTS), all with the
+ * same K; packed[i] int32 [M[i], K/8], scales[i] fp16 [M[i], K/128], y[i] fp16
+ * [B, M[i]].  The streaming kernel runs over the matrices' concatenated row
+ * tiles, so every output equals, bit for bit, a dk_w4a16_gemv of its matrix
+ * with the same config.  Version 5 or the reuse path; no counterpart in the
+ * reference, whose caller (w4a16_linear, python/decode_kernel/__init__.py:
+ * 62-83) launches one GEMV per matrix. */
+#define DK_MAX_SEGMENTS 4
+DK_API dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
+                                     const uint16_t* const* scales, const int* M,
+                                     uint16_t* const* y, const uint16_t* x, int K, int B,
+                                     const dk_gemv_config* cfg, void* stream);
+
 /* ------------------------------------------------------------------------
  * Sharded GEMV across the GPUs of one node (one process per GPU).  No
  * counterpart in the reference, which is single-GPU; these serve the

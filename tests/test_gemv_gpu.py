@@ -230,3 +230,35 @@ def test_batch_rows_9_to_32(B, shape, cuda_device):
     assert capi.load().dk_last_kernel_stamp(-1) == 15
     assert torch.equal(yr, y)
     assert capi.load().dk_device_error(-1, 0) == 0
+
+
+@pytest.mark.parametrize("B", [1, 3, 9, 33])
+@pytest.mark.parametrize("rows", [(4096, 4096, 4096), (11008, 11008), (17, 300, 1, 64), (1000,)])
+def test_multi_gemv_is_bitwise_the_separate_gemvs(rows, B, cuda_device):
+    # q/k/v- and gate/up-style launches: matrices sharing x, ragged row
+    # counts (partial last tiles inside the concatenation), several passes.
+    from decode_kernel import capi, gemv_multi
+
+    K = 2048
+    mats = [make_problem(m, K, 1, seed=900 + i + m, std=0.05)[:2] for i, m in enumerate(rows)]
+    x = np.random.default_rng(B).standard_normal((B, K)).astype(np.float16)
+    dev = [to_device(p, s, x) for p, s in mats]
+    tx = dev[0][2]
+    ys = gemv_multi([(tp, ts) for tp, ts, _ in dev], tx)
+    for (tp, ts, _), y, (p, s) in zip(dev, ys, mats):
+        assert torch.equal(y, capi_gemv(tp, ts, tx, cfg()))
+        if p.shape[0] * B <= 4096 * 3:
+            assert max_err(y, oracle_y(x, p, s)) < MAX_ABS
+    assert capi.load().dk_device_error(-1, 0) == 0
+
+
+def test_multi_gemv_rejects(cuda_device):
+    from decode_kernel import capi
+
+    c = cfg()
+    assert capi.gemv_multi([], [], [], [], 16, 256, 1, c) == capi.DK_ERR_INVALID_ARG
+    assert capi.gemv_multi([16] * 5, [16] * 5, [16] * 5, [16] * 5, 16, 256, 1, c) == \
+        capi.DK_ERR_INVALID_ARG
+    assert capi.gemv_multi([16], [16], [0], [16], 16, 256, 1, c) == capi.DK_ERR_INVALID_ARG
+    assert capi.gemv_multi([16], [16], [64], [16], 16, 256, 1, cfg(version=3)) == \
+        capi.DK_ERR_UNSUPPORTED
