@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(vb::kThreads, 1)
         if (lane < p.B) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < rows) store_y(p, lane, 0, r0 + c0 + j, acc[j]);
+            if (c0 + j < rows) store_y(p, lane, r0 + c0 + j, acc[j]);
         }
       }
       tcgen05_fence_before();
@@ -387,7 +387,7 @@ constexpr int kMinRows = 16384;
 template <int STAMP>
 dk_status launch_batch(GemvParams p, cudaStream_t st, bool pdl) {
   using namespace vb;
-  if (p.B <= 16 || p.B > kXRows || p.M < kMinRows || p.nseg != 1 || p.out.mode > kOutFloat ||
+  if (p.B <= 16 || p.B > kXRows || p.M < kMinRows || p.out.mode > kOutFloat ||
       p.ldx != p.K || p.K % kChunkK != 0)
     return DK_ERR_UNSUPPORTED;
   const int sms = sm_count(-1);

@@ -79,6 +79,11 @@ struct Segment {
   __half* y;               // [B, rows]
   int rows, tile0;
 };
+struct SegList {
+  int n;  // 2..kMaxSeg
+  Segment s[kMaxSeg];
+  __host__ __device__ int tiles() const { return s[n - 1].tile0 + (s[n - 1].rows + 15) / 16; }
+};
 
 struct GemvParams {
   const uint32_t* packed;  // [M, K/8]
@@ -86,8 +91,6 @@ struct GemvParams {
   const __half* x;         // [B, ldx]
   __half* y;               // [B, M]
   int M, K, B;
-  int nseg;                // v5: 1..kMaxSeg (1: seg[0] is packed/scales/y above)
-  Segment seg[kMaxSeg];
   int ldx;                 // row stride of x in elements (K, or more for a K slice)
   float* ws;               // v4: [K/128][B][M] fp32 per-group products
   unsigned* counters;      // v4: one arrival counter per 16-row tile
@@ -96,20 +99,60 @@ struct GemvParams {
   OutSpec out;             // v5: destination of y
 };
 
-// A global 16-row tile of a v5 call: its segment, first row inside the
-// segment and valid rows.
+// A CTA's share of a v5 call and its 16-row tiles.  One matrix: rows
+// [r0, r1) = [bid·M/grid, (bid+1)·M/grid) (the last tile may be partial).
+// Several matrices: whole global tiles [t0, t0 + ntiles) of the segments'
+// concatenation, each inside one segment.
 struct TileRef {
-  int seg, row, rows;
+  int seg, row, rows;  // segment, first row inside it, valid rows
 };
-__device__ __forceinline__ TileRef tile_ref(const GemvParams& p, int gtile) {
-  int s = 0;
-  while (s + 1 < p.nseg && gtile >= p.seg[s + 1].tile0) ++s;
-  const int row = (gtile - p.seg[s].tile0) * 16;
-  return {s, row, min(16, p.seg[s].rows - row)};
-}
+// v5 kernel argument besides GemvParams: the weights' tensor maps and, for
+// several matrices, their segments (kept out of GemvParams: a larger
+// GemvParams measurably slows the single-matrix kernel).
+template <bool MULTI>
+struct StreamArgs {
+  CUtensorMap m[1];
+};
+template <>
+struct StreamArgs<true> {
+  CUtensorMap m[kMaxSeg];
+  SegList segs;
+};
 
-// v5 result store for batch row b, output row m of segment seg.
-__device__ __forceinline__ void store_y(const GemvParams& p, int b, int seg, int m, float v) {
+template <bool MULTI>
+struct CtaTiles {
+  int r0, r1;     // one matrix
+  int t0;         // several matrices
+  int ntiles;
+  __device__ __forceinline__ void init(const GemvParams& p, const StreamArgs<MULTI>& a) {
+    if constexpr (!MULTI) {
+      r0 = (int)(((long long)blockIdx.x * p.M) / gridDim.x);
+      r1 = (int)(((long long)(blockIdx.x + 1) * p.M) / gridDim.x);
+      t0 = 0;
+      ntiles = (r1 - r0 + 15) / 16;
+    } else {
+      const int ntot = a.segs.tiles();
+      t0 = (int)(((long long)blockIdx.x * ntot) / gridDim.x);
+      ntiles = (int)(((long long)(blockIdx.x + 1) * ntot) / gridDim.x) - t0;
+      r0 = r1 = 0;
+    }
+  }
+  __device__ __forceinline__ TileRef operator()(const StreamArgs<MULTI>& a, int t) const {
+    if constexpr (!MULTI) {
+      const int row = r0 + t * 16;
+      return {0, row, min(16, r1 - row)};
+    } else {
+      const int gt = t0 + t;
+      int s = 0;
+      while (s + 1 < a.segs.n && gt >= a.segs.s[s + 1].tile0) ++s;
+      const int row = (gt - a.segs.s[s].tile0) * 16;
+      return {s, row, min(16, a.segs.s[s].rows - row)};
+    }
+  }
+};
+
+// v5 result store for batch row b, output row m.
+__device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v) {
   switch (p.out.mode) {
     case kOutFloat:
       static_cast<float*>(p.out.dst[0])[(size_t)b * p.M + m] = v;
@@ -125,7 +168,7 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int seg, int
         static_cast<float*>(p.out.dst[g])[((size_t)p.out.rank * p.B + b) * p.M + m] = v;
       break;
     default:
-      p.seg[seg].y[(size_t)b * p.seg[seg].rows + m] = __float2half_rn(v);
+      p.y[(size_t)b * p.M + m] = __float2half_rn(v);
   }
 }
 
@@ -727,14 +770,10 @@ __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
   }
 }
 
-// One tensor map per segment.
-struct TmapSet {
-  CUtensorMap m[kMaxSeg];
-};
 
-template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW, bool MULTI>
 __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
-    k_stream(const __grid_constant__ TmapSet tms, GemvParams p) {
+    k_stream(const __grid_constant__ StreamArgs<MULTI> a, GemvParams p) {
   using namespace v5;
   using CW = Consumers<NCW>;
   constexpr int kConsumerWarps = CW::kWarps;
@@ -760,10 +799,9 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   write_stamp(STAMP);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // This CTA's global tiles [t0, t0 + ntiles) of the segments' concatenation.
-  const int ntot = p.seg[p.nseg - 1].tile0 + (p.seg[p.nseg - 1].rows + 15) / 16;
-  const int t0 = (int)(((long long)blockIdx.x * ntot) / gridDim.x);
-  const int ntiles = (int)(((long long)(blockIdx.x + 1) * ntot) / gridDim.x) - t0;
+  CtaTiles<MULTI> tiles;
+  tiles.init(p, a);
+  const int ntiles = tiles.ntiles;
   const int groups = p.K / kGroup;
   const int nk = (groups + kChunkGroups - 1) / kChunkGroups;
   const int total = ntiles * nk;
@@ -782,8 +820,13 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     mbar_init(xready, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    if constexpr (TMAP)
-      for (int i = 0; i < p.nseg; ++i) tma_prefetch_desc(&tms.m[i]);
+    if constexpr (TMAP) {
+      if constexpr (MULTI) {
+        for (int i = 0; i < a.segs.n; ++i) tma_prefetch_desc(&a.m[i]);
+      } else {
+        tma_prefetch_desc(&a.m[0]);
+      }
+    }
   }
   __syncthreads();
   // A dependent GEMV launched with PDL may now start streaming its weights.
@@ -809,15 +852,26 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         bool go = !(XS && issued == kStagesBeforeX) || warp_test_wait(xready, 0);
         if (go && issued >= stages) go = warp_test_wait(&empty[cur.slot], (cur.round - 1) & 1);
         if (go) {
-          const TileRef tr = tile_ref(p, t0 + cur.tile);
-          const Segment& sg = p.seg[tr.seg];
+          const TileRef tr = tiles(a, cur.tile);
+          const CUtensorMap* tmap;
+          const __half* sscales;
+          const uint32_t* spacked;
+          if constexpr (MULTI) {
+            tmap = &a.m[tr.seg];
+            sscales = a.segs.s[tr.seg].scales;
+            spacked = a.segs.s[tr.seg].packed;
+          } else {
+            tmap = &a.m[0];
+            sscales = p.scales;
+            spacked = p.packed;
+          }
           const int trow = tr.row;
           const uint32_t dst = ring + cur.slot * kStageBytes;
           if constexpr (TMAP) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
-              tma_load_3d(dst, &tms.m[tr.seg], 0, trow, cur.chunk * kStripsPerChunk,
-                          &full[cur.slot], policy);
+              tma_load_3d(dst, tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot],
+                          policy);
             }
             // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups)
             // per cp.async.  K % 256 == 0 here, so scale rows are 4-byte
@@ -827,9 +881,11 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
-              if (r < tr.rows && gbase + w2 < groups)
+              // (one matrix: rows past this CTA's share are the next CTA's,
+              // in bounds and harmless)
+              if ((MULTI ? r < tr.rows : trow + r < p.M) && gbase + w2 < groups)
                 cp_async4(sdst + r * kScaleRowStride + w2 * 2,
-                          sg.scales + (size_t)(trow + r) * groups + gbase + w2);
+                          sscales + (size_t)(trow + r) * groups + gbase + w2);
             }
             cp_async_mbar_arrive(&full[cur.slot]);
           } else {
@@ -839,7 +895,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
             if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
             __syncwarp();
             if (lane < rows) {
-              const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(sg.packed);
+              const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(spacked);
               bulk_g2s(dst + lane * kPadRowStride,
                        wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
                        bytes, &full[cur.slot], policy);
@@ -855,7 +911,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         // Tile `reduced`: the 16 class partials of every real row and batch
         // column, added in class order.
         const float* rt = red + (reduced % kRedBufs) * kClasses * 16 * nbp;
-        const TileRef tr = tile_ref(p, t0 + reduced);
+        const TileRef tr = tiles(a, reduced);
         const int trow = tr.row, rows = tr.rows;
         const int nb = min(W, p.B);
         for (int o = lane; o < rows * nb; o += 32) {
@@ -864,7 +920,12 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
-          store_y(p, b, tr.seg, trow + r, sum);
+          if constexpr (MULTI) {
+            const Segment& sg = a.segs.s[tr.seg];
+            sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
+          } else {
+            store_y(p, b, trow + r, sum);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_free[reduced % kRedBufs]);
@@ -948,8 +1009,13 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   // Bulk path: scales from global memory, loaded one stage ahead.
   float sn[kGroupsPerWarp][2];
   auto load_scales = [&](const StageCursor& q) {
-    const TileRef tr = tile_ref(p, t0 + q.tile);
-    const __half* sp = p.seg[tr.seg].scales + (size_t)tr.row * groups;
+    const TileRef tr = tiles(a, q.tile);
+    const __half* sp;
+    if constexpr (MULTI) {
+      sp = a.segs.s[tr.seg].scales + (size_t)tr.row * groups;
+    } else {
+      sp = p.scales + (size_t)tr.row * groups;
+    }
 #pragma unroll
     for (int j = 0; j < kGroupsPerWarp; ++j) {
       const int G = min(q.chunk * kChunkGroups + warp + j * kConsumerWarps, groups - 1);
@@ -1153,8 +1219,9 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
   return true;
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP, int NCW>
-dk_status launch_stream_cfg(GemvParams p, const TmapSet& tmap, cudaStream_t st, bool pdl) {
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW, bool MULTI>
+dk_status launch_stream_cfg(GemvParams p, const StreamArgs<MULTI>& a, cudaStream_t st,
+                            bool pdl) {
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
@@ -1164,12 +1231,13 @@ dk_status launch_stream_cfg(GemvParams p, const TmapSet& tmap, cudaStream_t st, 
     --p.stages;
   const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total;
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
-  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW>, v5::kSmemCap, smem_done);
+  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, MULTI>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
-  const int tiles = p.seg[p.nseg - 1].tile0 + (p.seg[p.nseg - 1].rows + 15) / 16;
-  const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), tiles));
-  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW>, dim3(grid), dim3(NCW * 32 + 32),
-                smem, st, pdl, tmap, p);
+  int units = (p.M + 7) / 8;  // one matrix: >= 8 rows per CTA
+  if constexpr (MULTI) units = a.segs.tiles();
+  const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), units));
+  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, MULTI>, dim3(grid),
+                dim3(NCW * 32 + 32), smem, st, pdl, a, p);
 }
 
 // 8 consumer warps (two CTAs per SM) while a CTA's share of the weights is
@@ -1190,36 +1258,54 @@ bool use_coresident(const GemvParams& p) {
 #endif
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP>
-dk_status launch_stream_w(const GemvParams& p, const TmapSet& tmap, cudaStream_t st,
+template <int NT, int STAMP, bool XS, bool TMAP, bool MULTI>
+dk_status launch_stream_w(const GemvParams& p, const StreamArgs<MULTI>& a, cudaStream_t st,
                           bool pdl) {
   if constexpr (NT == 1 && XS) {
     if (use_coresident<NT, XS, TMAP>(p))
-      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8>(p, tmap, st, pdl);
+      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, MULTI>(p, a, st, pdl);
   }
-  return launch_stream_cfg<NT, STAMP, XS, TMAP, 16>(p, tmap, st, pdl);
+  return launch_stream_cfg<NT, STAMP, XS, TMAP, 16, MULTI>(p, a, st, pdl);
 }
 
 #include "dk_batch.cuh"
 
-template <int NT, int STAMP, bool TMAP>
-dk_status launch_stream_x(const GemvParams& p, const TmapSet& tmap, cudaStream_t st,
+template <int NT, int STAMP, bool TMAP, bool MULTI>
+dk_status launch_stream_x(const GemvParams& p, const StreamArgs<MULTI>& a, cudaStream_t st,
                           bool pdl) {
   if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
-    return launch_stream_w<1, STAMP, true, TMAP>(p, tmap, st, pdl);
-  return launch_stream_w<NT, STAMP, false, TMAP>(p, tmap, st, pdl);
+    return launch_stream_w<1, STAMP, true, TMAP, MULTI>(p, a, st, pdl);
+  return launch_stream_w<NT, STAMP, false, TMAP, MULTI>(p, a, st, pdl);
+}
+
+// The weights' tensor maps (TMA when every matrix has one; K % 256 keeps a
+// stage's 16 KB box whole), then the launch.  A single matrix (segs null)
+// runs the kernel compiled without segment indexing.
+template <int NT, int STAMP, bool MULTI>
+dk_status launch_stream_a(const GemvParams& p, StreamArgs<MULTI>& a, cudaStream_t st, bool pdl) {
+  bool tma = p.K % 256 == 0;
+  if constexpr (MULTI) {
+    for (int i = 0; tma && i < a.segs.n; ++i)
+      tma = weight_tensor_map(a.segs.s[i].packed, a.segs.s[i].rows, p.K, &a.m[i]);
+  } else {
+    tma = tma && weight_tensor_map(p.packed, p.M, p.K, &a.m[0]);
+  }
+  if (tma) return launch_stream_x<NT, STAMP, true, MULTI>(p, a, st, pdl);
+  std::memset(a.m, 0, sizeof(a.m));
+  return launch_stream_x<NT, STAMP, false, MULTI>(p, a, st, pdl);
 }
 
 template <int NT, int STAMP>
-dk_status launch_stream(const GemvParams& p, cudaStream_t st, bool pdl) {
-  TmapSet tmap;
-  std::memset(&tmap, 0, sizeof(tmap));
-  bool tma = p.K % 256 == 0;
-  for (int i = 0; tma && i < p.nseg; ++i)
-    tma = weight_tensor_map(p.seg[i].packed, p.seg[i].rows, p.K, &tmap.m[i]);
-  if (tma) return launch_stream_x<NT, STAMP, true>(p, tmap, st, pdl);
-  std::memset(&tmap, 0, sizeof(tmap));
-  return launch_stream_x<NT, STAMP, false>(p, tmap, st, pdl);
+dk_status launch_stream(const GemvParams& p, const SegList* segs, cudaStream_t st, bool pdl) {
+  if (segs) {
+    StreamArgs<true> a;
+    std::memset(&a, 0, sizeof(a));
+    a.segs = *segs;
+    return launch_stream_a<NT, STAMP, true>(p, a, st, pdl);
+  }
+  StreamArgs<false> a;
+  std::memset(&a, 0, sizeof(a));
+  return launch_stream_a<NT, STAMP, false>(p, a, st, pdl);
 }
 
 template <int NT, int MODE>
@@ -1246,15 +1332,17 @@ dk_status launch_tile_nt(const GemvParams& p, int split, cudaStream_t st, bool p
   return launch_tile<4, MODE>(p, split, st, pdl);
 }
 
+// segs: several matrices sharing x (null: the one matrix of p).
 template <int STAMP>
-dk_status launch_stream_nt(const GemvParams& p, cudaStream_t st, bool pdl) {
-  if (p.B <= 8) return launch_stream<1, STAMP>(p, st, pdl);
-  {
+dk_status launch_stream_nt(const GemvParams& p, cudaStream_t st, bool pdl,
+                           const SegList* segs = nullptr) {
+  if (p.B <= 8) return launch_stream<1, STAMP>(p, segs, st, pdl);
+  if (!segs) {
     const dk_status b = launch_batch<STAMP>(p, st, pdl);  // tensor cores, large W, 17..32 rows
     if (b != DK_ERR_UNSUPPORTED) return b;
   }
-  if (p.B <= 16) return launch_stream<2, STAMP>(p, st, pdl);
-  return launch_stream<4, STAMP>(p, st, pdl);
+  if (p.B <= 16) return launch_stream<2, STAMP>(p, segs, st, pdl);
+  return launch_stream<4, STAMP>(p, segs, st, pdl);
 }
 
 // v4 workspace: one arrival counter per 16-row tile (padded to 256 B), then
@@ -1286,12 +1374,6 @@ extern "C" void dk_gemv_config_init(dk_gemv_config* cfg) {
   cfg->reuse_weights = 0;
   cfg->warps_per_row = 1;
   cfg->flags = 0;
-}
-
-// One weight matrix: segment 0 is (packed, scales, y, M).
-static void single_segment(GemvParams& p) {
-  p.nseg = 1;
-  p.seg[0] = Segment{p.packed, p.scales, p.y, p.M, 0};
 }
 
 static dk_status validate_config(const dk_gemv_config& c) {
@@ -1387,7 +1469,6 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
     }
     p.ws = partials;
     p.counters = counters;
-    single_segment(p);
     if (c.reuse_weights) {
       s = launch_stream_nt<kStampReuse>(p, st, pdl);
     } else {
@@ -1476,15 +1557,18 @@ extern "C" dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
     p.B = std::min(kMaxBatchPerPass, B - b0);
     p.ws = nullptr;
     p.counters = nullptr;
-    p.nseg = n;
+    SegList segs;
+    segs.n = n;
     int tile0 = 0;
     for (int i = 0; i < n; ++i) {
-      p.seg[i] = Segment{reinterpret_cast<const uint32_t*>(packed[i]),
+      segs.s[i] = Segment{reinterpret_cast<const uint32_t*>(packed[i]),
                          reinterpret_cast<const __half*>(scales[i]),
                          reinterpret_cast<__half*>(y[i]) + (size_t)b0 * M[i], M[i], tile0};
       tile0 += (M[i] + 15) / 16;
     }
-    s = c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl) : launch_stream_nt<5>(p, st, pdl);
+    const SegList* sl = n > 1 ? &segs : nullptr;  // one matrix: p already describes it
+    s = c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl, sl)
+                        : launch_stream_nt<5>(p, st, pdl, sl);
     if (s != DK_OK) return s;
   }
   return DK_OK;
@@ -1529,7 +1613,6 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   p.ws = nullptr;
   p.counters = nullptr;
   p.y = nullptr;
-  single_segment(p);
   const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
   return c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl)
                          : launch_stream_nt<5>(p, st, pdl);
