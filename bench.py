@@ -43,8 +43,9 @@ for _p in (str(REPO), str(REPO / "decode-kernel_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-METRIC = ("achieved HBM read GB/s (% of measured B200 read roof) and µs/GEMV, "
-          "4096x4096 B=1")
+def metric_name(m: int, k: int, b: int) -> str:
+    return ("achieved HBM read GB/s (% of measured B200 read roof) and µs/GEMV, "
+            f"{m}x{k} B={b}")
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -76,10 +77,10 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic_per_launch():
+def ncu_traffic_per_launch(m: int, k: int, b: int):
     """dram read+write bytes per launch of the dominant kernel, from the
-    committed ncu summary (profiles/), or None."""
-    p = REPO / "profiles" / "k_stream_4096x4096_b1.md"
+    committed ncu summary of this workload (profiles/), or None."""
+    p = REPO / "profiles" / f"k_stream_{m}x{k}_b{b}.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -236,7 +237,7 @@ def run_reference(args) -> None:
     cores = O.cpu_threads()
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": metric_name(M, K, B),
         "value": gbs,
         "unit": "GB/s",
         "n_gpus": ws,
@@ -412,10 +413,10 @@ def run_ours(args) -> None:
     if rank != 0:
         return
     peak, peak_kind = measured_peaks()
-    traffic = ncu_traffic_per_launch()
+    traffic = ncu_traffic_per_launch(M, K, B)
     clk = clocks.summary()
     line = {
-        "metric": METRIC,
+        "metric": metric_name(M, K, B),
         "value": value,
         "unit": "GB/s",
         "n_gpus": ws,
