@@ -79,10 +79,19 @@ struct Segment {
   __half* y;               // [B, rows]
   int rows, tile0;
 };
+// Paired (gate/up SiLU-mul) mode: n == 2 with equal rows; the tiles run as
+// (gate tile j, up tile j) pairs, CTAs own whole pairs, and only s[0].y --
+// h = silu(gate) * up -- is written.
 struct SegList {
-  int n;  // 2..kMaxSeg
+  int n;       // 2..kMaxSeg
+  int paired;  // 1: gate/up SiLU-mul pairs
   Segment s[kMaxSeg];
-  __host__ __device__ int tiles() const { return s[n - 1].tile0 + (s[n - 1].rows + 15) / 16; }
+  __host__ __device__ int pairs() const { return (s[0].rows + 15) / 16; }
+  __host__ __device__ int tiles() const {
+    return paired ? 2 * pairs() : s[n - 1].tile0 + (s[n - 1].rows + 15) / 16;
+  }
+  // Units the CTAs split: pairs, or tiles.
+  __host__ __device__ int units() const { return paired ? pairs() : tiles(); }
 };
 
 struct GemvParams {
@@ -106,6 +115,10 @@ struct GemvParams {
 struct TileRef {
   int seg, row, rows;  // segment, first row inside it, valid rows
 };
+// Segment modes of the v5 kernel (compile-time, so the single-matrix kernel
+// carries no segment code): one matrix, several, gate/up SiLU-mul pairs.
+constexpr int kSegOne = 0, kSegMulti = 1, kSegPair = 2;
+
 // v5 kernel argument besides GemvParams: the weights' tensor maps and, for
 // several matrices, their segments (kept out of GemvParams: a larger
 // GemvParams measurably slows the single-matrix kernel).
@@ -119,8 +132,9 @@ struct StreamArgs<true> {
   SegList segs;
 };
 
-template <bool MULTI>
+template <int SEG>
 struct CtaTiles {
+  static constexpr bool MULTI = SEG != kSegOne;
   int r0, r1;     // one matrix
   int t0;         // several matrices
   int ntiles;
@@ -131,9 +145,13 @@ struct CtaTiles {
       t0 = 0;
       ntiles = (r1 - r0 + 15) / 16;
     } else {
-      const int ntot = a.segs.tiles();
+      const int ntot = a.segs.units();
       t0 = (int)(((long long)blockIdx.x * ntot) / gridDim.x);
       ntiles = (int)(((long long)(blockIdx.x + 1) * ntot) / gridDim.x) - t0;
+      if constexpr (SEG == kSegPair) {
+        t0 *= 2;
+        ntiles *= 2;
+      }
       r0 = r1 = 0;
     }
   }
@@ -143,6 +161,10 @@ struct CtaTiles {
       return {0, row, min(16, r1 - row)};
     } else {
       const int gt = t0 + t;
+      if constexpr (SEG == kSegPair) {
+        const int row = (gt >> 1) * 16;
+        return {gt & 1, row, min(16, a.segs.s[0].rows - row)};
+      }
       int s = 0;
       while (s + 1 < a.segs.n && gt >= a.segs.s[s + 1].tile0) ++s;
       const int row = (gt - a.segs.s[s].tile0) * 16;
@@ -771,10 +793,11 @@ __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
 }
 
 
-template <int NT, int STAMP, bool XS, bool TMAP, int NCW, bool MULTI>
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW, int SEG>
 __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
-    k_stream(const __grid_constant__ StreamArgs<MULTI> a, GemvParams p) {
+    k_stream(const __grid_constant__ StreamArgs<SEG != kSegOne> a, GemvParams p) {
   using namespace v5;
+  constexpr bool MULTI = SEG != kSegOne;
   using CW = Consumers<NCW>;
   constexpr int kConsumerWarps = CW::kWarps;
   constexpr int kConsumerThreads = CW::kThreads;
@@ -799,7 +822,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   write_stamp(STAMP);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  CtaTiles<MULTI> tiles;
+  CtaTiles<SEG> tiles;
   tiles.init(p, a);
   const int ntiles = tiles.ntiles;
   const int groups = p.K / kGroup;
@@ -914,21 +937,47 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         const TileRef tr = tiles(a, reduced);
         const int trow = tr.row, rows = tr.rows;
         const int nb = min(W, p.B);
-        for (int o = lane; o < rows * nb; o += 32) {
-          const int r = o / nb, b = o - r * nb;
-          const float* src = rt + r * nbp + b;
-          float sum = 0.f;
+        constexpr bool paired = SEG == kSegPair;
+        if (paired && tr.seg == 0) {
+          // Gate tile: its partials stay in their buffer until the up tile
+          // of the same rows has been added up too.
+        } else {
+          for (int o = lane; o < rows * nb; o += 32) {
+            const int r = o / nb, b = o - r * nb;
+            const float* src = rt + r * nbp + b;
+            float sum = 0.f;
 #pragma unroll
-          for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
-          if constexpr (MULTI) {
-            const Segment& sg = a.segs.s[tr.seg];
-            sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
-          } else {
-            store_y(p, b, trow + r, sum);
+            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
+            if constexpr (MULTI) {
+              if (paired) {
+                // h = silu(g) * u with the roundings of the unfused fp16
+                // sequence: g and u as GEMV outputs, silu(g) = g / (1 +
+                // exp(-g)) in fp32 rounded to fp16, the product in fp32
+                // rounded to fp16.
+                const float* gsrc =
+                    red + ((reduced - 1) % kRedBufs) * kClasses * 16 * nbp + r * nbp + b;
+                float gsum = 0.f;
+#pragma unroll
+                for (int w = 0; w < kClasses; ++w) gsum = __fadd_rn(gsum, gsrc[w * 16 * nbp]);
+                const float g = __half2float(__float2half_rn(gsum));
+                const float sg = __half2float(__float2half_rn(g / (1.0f + expf(-g))));
+                const float u = __half2float(__float2half_rn(sum));
+                const Segment& s0 = a.segs.s[0];
+                s0.y[(size_t)b * s0.rows + trow + r] = __float2half_rn(__fmul_rn(sg, u));
+              } else {
+                const Segment& sg = a.segs.s[tr.seg];
+                sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
+              }
+            } else {
+              store_y(p, b, trow + r, sum);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            if (paired) mbar_arrive(&red_free[(reduced - 1) % kRedBufs]);
+            mbar_arrive(&red_free[reduced % kRedBufs]);
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&red_free[reduced % kRedBufs]);
         ++reduced;
         progress = true;
       }
@@ -1219,8 +1268,8 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
   return true;
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP, int NCW, bool MULTI>
-dk_status launch_stream_cfg(GemvParams p, const StreamArgs<MULTI>& a, cudaStream_t st,
+template <int NT, int STAMP, bool XS, bool TMAP, int NCW, int SEG>
+dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                             bool pdl) {
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
@@ -1231,12 +1280,12 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<MULTI>& a, cudaStream
     --p.stages;
   const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total;
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
-  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, MULTI>, v5::kSmemCap, smem_done);
+  dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
   int units = (p.M + 7) / 8;  // one matrix: >= 8 rows per CTA
-  if constexpr (MULTI) units = a.segs.tiles();
+  if constexpr (SEG != kSegOne) units = a.segs.units();
   const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), units));
-  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, MULTI>, dim3(grid),
+  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, dim3(grid),
                 dim3(NCW * 32 + 32), smem, st, pdl, a, p);
 }
 
@@ -1258,41 +1307,42 @@ bool use_coresident(const GemvParams& p) {
 #endif
 }
 
-template <int NT, int STAMP, bool XS, bool TMAP, bool MULTI>
-dk_status launch_stream_w(const GemvParams& p, const StreamArgs<MULTI>& a, cudaStream_t st,
+template <int NT, int STAMP, bool XS, bool TMAP, int SEG>
+dk_status launch_stream_w(const GemvParams& p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                           bool pdl) {
   if constexpr (NT == 1 && XS) {
     if (use_coresident<NT, XS, TMAP>(p))
-      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, MULTI>(p, a, st, pdl);
+      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, SEG>(p, a, st, pdl);
   }
-  return launch_stream_cfg<NT, STAMP, XS, TMAP, 16, MULTI>(p, a, st, pdl);
+  return launch_stream_cfg<NT, STAMP, XS, TMAP, 16, SEG>(p, a, st, pdl);
 }
 
 #include "dk_batch.cuh"
 
-template <int NT, int STAMP, bool TMAP, bool MULTI>
-dk_status launch_stream_x(const GemvParams& p, const StreamArgs<MULTI>& a, cudaStream_t st,
+template <int NT, int STAMP, bool TMAP, int SEG>
+dk_status launch_stream_x(const GemvParams& p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                           bool pdl) {
   if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
-    return launch_stream_w<1, STAMP, true, TMAP, MULTI>(p, a, st, pdl);
-  return launch_stream_w<NT, STAMP, false, TMAP, MULTI>(p, a, st, pdl);
+    return launch_stream_w<1, STAMP, true, TMAP, SEG>(p, a, st, pdl);
+  return launch_stream_w<NT, STAMP, false, TMAP, SEG>(p, a, st, pdl);
 }
 
 // The weights' tensor maps (TMA when every matrix has one; K % 256 keeps a
 // stage's 16 KB box whole), then the launch.  A single matrix (segs null)
 // runs the kernel compiled without segment indexing.
-template <int NT, int STAMP, bool MULTI>
-dk_status launch_stream_a(const GemvParams& p, StreamArgs<MULTI>& a, cudaStream_t st, bool pdl) {
+template <int NT, int STAMP, int SEG>
+dk_status launch_stream_a(const GemvParams& p, StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
+                          bool pdl) {
   bool tma = p.K % 256 == 0;
-  if constexpr (MULTI) {
+  if constexpr (SEG != kSegOne) {
     for (int i = 0; tma && i < a.segs.n; ++i)
       tma = weight_tensor_map(a.segs.s[i].packed, a.segs.s[i].rows, p.K, &a.m[i]);
   } else {
     tma = tma && weight_tensor_map(p.packed, p.M, p.K, &a.m[0]);
   }
-  if (tma) return launch_stream_x<NT, STAMP, true, MULTI>(p, a, st, pdl);
+  if (tma) return launch_stream_x<NT, STAMP, true, SEG>(p, a, st, pdl);
   std::memset(a.m, 0, sizeof(a.m));
-  return launch_stream_x<NT, STAMP, false, MULTI>(p, a, st, pdl);
+  return launch_stream_x<NT, STAMP, false, SEG>(p, a, st, pdl);
 }
 
 template <int NT, int STAMP>
@@ -1301,11 +1351,12 @@ dk_status launch_stream(const GemvParams& p, const SegList* segs, cudaStream_t s
     StreamArgs<true> a;
     std::memset(&a, 0, sizeof(a));
     a.segs = *segs;
-    return launch_stream_a<NT, STAMP, true>(p, a, st, pdl);
+    if (segs->paired) return launch_stream_a<NT, STAMP, kSegPair>(p, a, st, pdl);
+    return launch_stream_a<NT, STAMP, kSegMulti>(p, a, st, pdl);
   }
   StreamArgs<false> a;
   std::memset(&a, 0, sizeof(a));
-  return launch_stream_a<NT, STAMP, false>(p, a, st, pdl);
+  return launch_stream_a<NT, STAMP, kSegOne>(p, a, st, pdl);
 }
 
 template <int NT, int MODE>
@@ -1558,6 +1609,7 @@ extern "C" dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
     p.ws = nullptr;
     p.counters = nullptr;
     SegList segs;
+    std::memset(&segs, 0, sizeof(segs));
     segs.n = n;
     int tile0 = 0;
     for (int i = 0; i < n; ++i) {
@@ -1569,6 +1621,69 @@ extern "C" dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
     const SegList* sl = n > 1 ? &segs : nullptr;  // one matrix: p already describes it
     s = c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl, sl)
                         : launch_stream_nt<5>(p, st, pdl, sl);
+    if (s != DK_OK) return s;
+  }
+  return DK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Gate/up pair with the SiLU-mul epilogue: h = silu(x . Wg^T) * (x . Wu^T),
+// the two GEMVs in one launch over (gate tile, up tile) pairs.
+// ---------------------------------------------------------------------------
+extern "C" dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate,
+                                            const uint16_t* scales_gate,
+                                            const int32_t* packed_up, const uint16_t* scales_up,
+                                            const uint16_t* x, uint16_t* h, int M, int K, int B,
+                                            const dk_gemv_config* cfg, void* stream) {
+  dk_gemv_config c;
+  dk_gemv_config_init(&c);
+  if (cfg) c = *cfg;
+  dk_status s = validate_config(c);
+  if (s != DK_OK) return s;
+  if (c.flags & DK_FLAG_SHARD_WAIT) return DK_ERR_INVALID_ARG;
+  if (M < 1 || K < 0 || B < 0 || K % DK_GROUP_SIZE != 0 || !packed_gate || !scales_gate ||
+      !packed_up || !scales_up || !h)
+    return DK_ERR_INVALID_ARG;
+  if ((c.version != 5 && !c.reuse_weights) || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
+  if (K > 0 && (!aligned16(packed_gate) || !aligned16(packed_up) ||
+                ((reinterpret_cast<uintptr_t>(scales_gate) | reinterpret_cast<uintptr_t>(scales_up)) & 1u)))
+    return DK_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(h) & 1u) return DK_ERR_INVALID_ARG;
+  if (2ll * M > (1ll << 30)) return DK_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0) return DK_OK;
+  if (K == 0) {  // gate = up = 0, silu(0) * 0 = 0
+    const cudaError_t e = cudaMemsetAsync(h, 0, (size_t)B * M * sizeof(uint16_t), st);
+    if (e != cudaSuccess) {
+      set_cuda_error(e, "cudaMemsetAsync");
+      return DK_ERR_CUDA;
+    }
+    return DK_OK;
+  }
+  if (!x || !aligned16(x)) return DK_ERR_INVALID_ARG;
+  const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
+  for (int b0 = 0; b0 < B; b0 += kMaxBatchPerPass) {
+    GemvParams p;
+    p.packed = reinterpret_cast<const uint32_t*>(packed_gate);
+    p.scales = reinterpret_cast<const __half*>(scales_gate);
+    p.x = reinterpret_cast<const __half*>(x) + (size_t)b0 * K;
+    p.y = reinterpret_cast<__half*>(h) + (size_t)b0 * M;
+    p.M = 2 * M;  // rows streamed
+    p.K = K;
+    p.ldx = K;
+    p.B = std::min(kMaxBatchPerPass, B - b0);
+    p.ws = nullptr;
+    p.counters = nullptr;
+    SegList segs;
+    std::memset(&segs, 0, sizeof(segs));
+    segs.n = 2;
+    segs.paired = 1;
+    segs.s[0] = Segment{reinterpret_cast<const uint32_t*>(packed_gate),
+                        reinterpret_cast<const __half*>(scales_gate), p.y, M, 0};
+    segs.s[1] = Segment{reinterpret_cast<const uint32_t*>(packed_up),
+                        reinterpret_cast<const __half*>(scales_up), nullptr, M, 0};
+    s = c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl, &segs)
+                        : launch_stream_nt<5>(p, st, pdl, &segs);
     if (s != DK_OK) return s;
   }
   return DK_OK;

@@ -23,6 +23,7 @@ __all__ = [
     "W4A16Linear",
     "cuda_available",
     "gemv_multi",
+    "gemv_silu_mul",
     "dequantize",
     "gemv",
     "gemv_out",
@@ -128,6 +129,46 @@ def gemv_multi(weights, x: torch.Tensor, pdl: bool = False, reuse_weights: bool 
                                torch.cuda.current_stream(x.device).cuda_stream),
                "dk_w4a16_gemv_multi")
     return ys
+
+
+def _check_pair(packed: torch.Tensor, scales: torch.Tensor, K: int) -> None:
+    if packed.dtype != torch.int32 or scales.dtype != torch.float16 or not (
+            packed.is_cuda and scales.is_cuda):
+        raise RuntimeError("packed must be CUDA int32 and scales CUDA fp16")
+    if packed.dim() != 2 or packed.shape[1] * 8 != K or scales.shape != (packed.shape[0],
+                                                                          K // GROUP_SIZE):
+        raise RuntimeError("every matrix must be [M, K/8] with scales [M, K/128] for x's K")
+    if not (packed.is_contiguous() and scales.is_contiguous()):
+        raise RuntimeError("packed and scales must be contiguous")
+
+
+def gemv_silu_mul(gate, up, x: torch.Tensor, pdl: bool = False, reuse_weights: bool = False):
+    """The gate/up pair of a gated MLP with its SiLU-mul epilogue, one launch.
+
+    ``gate`` and ``up``: ``(packed, scales)`` of two [M, K] matrices.  Returns
+    fp16 [B, M] ``h = silu(gemv(gate, x)) * gemv(up, x)`` with the roundings of
+    that unfused fp16 sequence (``torch.nn.functional.silu`` then ``*``).
+    """
+    from . import capi
+
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if x.dtype != torch.float16 or not x.is_cuda or not x.is_contiguous() or x.dim() != 2:
+        raise RuntimeError("x must be a contiguous 2-D CUDA fp16 tensor")
+    K = x.shape[1]
+    _check_pair(*gate, K)
+    _check_pair(*up, K)
+    if gate[0].shape != up[0].shape:
+        raise RuntimeError("gate and up must have the same shape")
+    M = gate[0].shape[0]
+    h = torch.empty((x.shape[0], M), dtype=torch.float16, device=x.device)
+    flags = capi.DK_FLAG_PDL if pdl else 0
+    cfg = capi.default_config(reuse_weights=int(bool(reuse_weights)), flags=flags)
+    capi.check(capi.gemv_silu_mul(gate[0].data_ptr(), gate[1].data_ptr(), up[0].data_ptr(),
+                                  up[1].data_ptr(), x.data_ptr(), h.data_ptr(), M, K, x.shape[0],
+                                  cfg, torch.cuda.current_stream(x.device).cuda_stream),
+               "dk_w4a16_gemv_silu_mul")
+    return h
 
 
 def w4a16_linear(

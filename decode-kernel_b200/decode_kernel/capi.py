@@ -66,6 +66,8 @@ SIGNATURES = {
     "dk_w4a16_gemv_splitk_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "dk_w4a16_gemv_multi": (_I, [_I, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_I),
                                  ctypes.POINTER(_P), _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
+    "dk_w4a16_gemv_silu_mul": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I,
+                                    ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_rowshard": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
                                     ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_kshard": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
@@ -145,6 +147,16 @@ def gemv(packed_ptr: int, scales_ptr: int, x_ptr: int, y_ptr: int, M: int, K: in
 def workspace_bytes(M: int, K: int, B: int, cfg: GemvConfig | None = None) -> int:
     return int(load().dk_w4a16_workspace_bytes(M, K, B,
                                                ctypes.byref(cfg) if cfg is not None else None))
+
+
+def gemv_silu_mul(packed_gate: int, scales_gate: int, packed_up: int, scales_up: int,
+                  x_ptr: int, h_ptr: int, M: int, K: int, B: int,
+                  cfg: GemvConfig | None = None, stream: int = 0) -> int:
+    """dk_w4a16_gemv_silu_mul over device addresses; returns the status."""
+    return load().dk_w4a16_gemv_silu_mul(packed_gate, scales_gate, packed_up, scales_up, x_ptr,
+                                         h_ptr, M, K, B,
+                                         ctypes.byref(cfg) if cfg is not None else None,
+                                         stream or None)
 
 
 def gemv_multi(packed_ptrs, scales_ptrs, Ms, y_ptrs, x_ptr: int, K: int, B: int,

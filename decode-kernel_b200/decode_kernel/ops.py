@@ -7,7 +7,9 @@ side of the reference's ``w4a16_linear``, python/decode_kernel/__init__.py:
 -- torch.fx, ``torch.cuda.CUDAGraph`` capture of a decode step -- sees a
 proper operator with a known output shape instead of an opaque Python call.
 ``W4A16Linear`` is a bias-free ``nn.Linear`` replacement holding the packed
-weights and scales as buffers.
+weights and scales as buffers.  ``torch.ops.decode_kernel.w4a16_silu_mul(x,
+packed_gate, scales_gate, packed_up, scales_up)`` is a gated MLP's gate/up
+pair with its SiLU-mul epilogue in one launch.
 
 There is no CPU implementation: the op raises on CPU tensors, like the rest of
 the package.
@@ -21,7 +23,7 @@ import torch
 
 from .quantize import GROUP_SIZE, quantize_and_pack_cuda
 
-__all__ = ["W4A16Linear", "w4a16_linear_op"]
+__all__ = ["W4A16Linear", "w4a16_linear_op", "w4a16_silu_mul_op"]
 
 
 @torch.library.custom_op("decode_kernel::w4a16_linear", mutates_args=())
@@ -42,6 +44,28 @@ def _(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor) -> torch.Tens
     torch._check(x.shape[-1] == packed.shape[1] * 8, lambda: "x.shape[-1] must equal K")
     torch._check(x.dtype == torch.float16, lambda: "x must be fp16")
     return x.new_empty((*x.shape[:-1], packed.shape[0]), dtype=torch.float16)
+
+
+@torch.library.custom_op("decode_kernel::w4a16_silu_mul", mutates_args=())
+def w4a16_silu_mul_op(x: torch.Tensor, packed_gate: torch.Tensor, scales_gate: torch.Tensor,
+                      packed_up: torch.Tensor, scales_up: torch.Tensor) -> torch.Tensor:
+    """h[..., M] = silu(x . Wg^T) * (x . Wu^T) (fp16), one launch for both GEMVs."""
+    from . import gemv_silu_mul
+
+    if not x.is_cuda:
+        raise RuntimeError("decode_kernel::w4a16_silu_mul runs on CUDA tensors only")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    h = gemv_silu_mul((packed_gate, scales_gate), (packed_up, scales_up), x2)
+    return h.reshape(*lead, packed_gate.shape[0])
+
+
+@w4a16_silu_mul_op.register_fake
+def _(x, packed_gate, scales_gate, packed_up, scales_up):
+    torch._check(x.shape[-1] == packed_gate.shape[1] * 8, lambda: "x.shape[-1] must equal K")
+    torch._check(packed_up.shape[0] == packed_gate.shape[0], lambda: "gate and up rows differ")
+    torch._check(x.dtype == torch.float16, lambda: "x must be fp16")
+    return x.new_empty((*x.shape[:-1], packed_gate.shape[0]), dtype=torch.float16)
 
 
 class W4A16Linear(torch.nn.Module):

@@ -153,6 +153,20 @@ DK_API dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
                                      uint16_t* const* y, const uint16_t* x, int K, int B,
                                      const dk_gemv_config* cfg, void* stream);
 
+/* The gate/up pair of a gated MLP with its SiLU-mul epilogue in one launch:
+ * h[b, m] = silu(g) * u with g = x . dequant(W_gate)^T, u = x . dequant(W_up)^T
+ * (both [M, K]; h fp16 [B, M]).  The roundings are those of the unfused
+ * sequence -- g and u as fp16 GEMV outputs (bit for bit dk_w4a16_gemv),
+ * silu(g) = g / (1 + exp(-g)) in fp32 rounded to fp16, the product in fp32
+ * rounded to fp16 -- so h equals silu(gemv(W_gate, x)) * gemv(W_up, x)
+ * computed elementwise in fp16.  Version 5 or the reuse path.  The caller side
+ * of the reference's w4a16_linear (python/decode_kernel/__init__.py:62-83)
+ * makes two GEMV calls and an elementwise op for this. */
+DK_API dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate, const uint16_t* scales_gate,
+                                        const int32_t* packed_up, const uint16_t* scales_up,
+                                        const uint16_t* x, uint16_t* h, int M, int K, int B,
+                                        const dk_gemv_config* cfg, void* stream);
+
 /* ------------------------------------------------------------------------
  * Sharded GEMV across the GPUs of one node (one process per GPU).  No
  * counterpart in the reference, which is single-GPU; these serve the

@@ -262,3 +262,55 @@ def test_multi_gemv_rejects(cuda_device):
     assert capi.gemv_multi([16], [16], [0], [16], 16, 256, 1, c) == capi.DK_ERR_INVALID_ARG
     assert capi.gemv_multi([16], [16], [64], [16], 16, 256, 1, cfg(version=3)) == \
         capi.DK_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("reuse", [False, True])
+@pytest.mark.parametrize("shape", [(11008, 4096, 1), (4096, 4096, 4), (1000, 256, 3), (17, 128, 1),
+                                   (4096, 1024, 16), (2000, 2048, 32), (300, 1024, 40)])
+def test_silu_mul_is_the_unfused_fp16_sequence(shape, reuse, cuda_device):
+    # Gate/up with the SiLU-mul epilogue: bitwise the unfused sequence (two
+    # GEMVs, torch's silu, fp16 product), and within the propagated oracle
+    # bound.  Ragged M (partial last pair), several batch passes (B=40).
+    import torch.nn.functional as F
+
+    from decode_kernel import gemv_silu_mul
+
+    M, K, B = shape
+    pg, sg, x = make_problem(M, K, B, seed=1300 + M + B, std=0.05)
+    pu, su, _ = make_problem(M, K, 1, seed=1400 + M + B, std=0.05)
+    tg, tsg, tx = to_device(pg, sg, x)
+    tu, tsu, _ = to_device(pu, su, x)
+    h = gemv_silu_mul((tg, tsg), (tu, tsu), tx, reuse_weights=reuse)
+    c = cfg(reuse_weights=int(reuse))
+    g16, u16 = capi_gemv(tg, tsg, tx, c), capi_gemv(tu, tsu, tx, c)
+    assert torch.equal(h, F.silu(g16) * u16)
+    if M * B <= 4096 * 4:
+        g, u = oracle_y(x, pg, sg).astype(np.float64), oracle_y(x, pu, su).astype(np.float64)
+        s = g / (1.0 + np.exp(-g))
+        ref = s * u
+        hh = h.float().cpu().numpy()
+        assert np.isfinite(hh).all()
+        bound = 1.2e-2 * (np.abs(u) + np.abs(s)) + 1e-3 * np.abs(ref) + 1e-3
+        assert (np.abs(hh - ref) <= bound).all()
+    from decode_kernel import capi
+
+    assert capi.load().dk_device_error(-1, 0) == 0
+
+
+def test_silu_mul_rejects(cuda_device):
+    from decode_kernel import capi, gemv_silu_mul
+
+    c = cfg()
+    f = capi.gemv_silu_mul
+    assert f(16, 16, 16, 16, 16, 16, 0, 256, 1, c) == capi.DK_ERR_INVALID_ARG       # M < 1
+    assert f(16, 16, 16, 16, 16, 16, 64, 200, 1, c) == capi.DK_ERR_INVALID_ARG      # K % 128
+    assert f(16, 16, 16, 16, 16, 16, 64, 256, 1, cfg(version=3)) == capi.DK_ERR_UNSUPPORTED
+    assert f(16, 16, 16, 16, 16, 16, 64, 256, 1, cfg(flags=capi.DK_FLAG_F32_OUT)) == \
+        capi.DK_ERR_UNSUPPORTED
+    assert f(16, 16, 16, 16, 16, 16, 64, 256, 0, c) == capi.DK_OK                  # B = 0
+    pg, sg, x = make_problem(64, 256, 2, seed=5)
+    tg, tsg, tx = to_device(pg, sg, x)
+    pu, su, _ = make_problem(32, 256, 1, seed=6)
+    tu, tsu, _ = to_device(pu, su, x)
+    with pytest.raises(RuntimeError):
+        gemv_silu_mul((tg, tsg), (tu, tsu), tx)  # different M

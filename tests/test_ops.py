@@ -87,3 +87,32 @@ def test_from_linear_and_graph_captured_stack(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(static_y, stack(x * scale))
     assert torch.equal(stack(x), eager)
+
+
+def test_silu_mul_operator_fake_shape():
+    import decode_kernel  # noqa: F401  (registers the op)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    assert hasattr(torch.ops.decode_kernel, "w4a16_silu_mul")
+    with FakeTensorMode():
+        x = torch.empty(2, 3, 256, dtype=torch.float16)
+        pg = torch.empty(96, 32, dtype=torch.int32)
+        sg = torch.empty(96, 2, dtype=torch.float16)
+        h = torch.ops.decode_kernel.w4a16_silu_mul(x, pg, sg, pg, sg)
+        assert h.shape == (2, 3, 96) and h.dtype == torch.float16
+
+
+@pytest.mark.gpu
+def test_silu_mul_operator_matches_unfused_and_opcheck(cuda_device):
+    import torch.nn.functional as F
+
+    from decode_kernel import gemv
+
+    pg, sg, x = make_problem(200, 512, 3, seed=91, std=0.05)
+    pu, su, _ = make_problem(200, 512, 1, seed=92, std=0.05)
+    tg, tsg, tx = to_device(pg, sg, x)
+    tu, tsu, _ = to_device(pu, su, x)
+    h = torch.ops.decode_kernel.w4a16_silu_mul(tx.reshape(1, 3, 512), tg, tsg, tu, tsu)
+    assert torch.equal(h.reshape(3, 200), F.silu(gemv(tg, tsg, tx)) * gemv(tu, tsu, tx))
+    torch.library.opcheck(torch.ops.decode_kernel.w4a16_silu_mul.default, (tx, tg, tsg, tu, tsu),
+                          test_utils=("test_schema", "test_faketensor"))
