@@ -14,9 +14,10 @@ value   device-resident throughput: the step is captured once in a CUDA
         graph (GEMVs launched through the C ABI with programmatic dependent
         launch, so each kernel's weight stream overlaps its predecessor's
         tail) and replayed K times between CUDA events.
-e2e     the same metric through the public Python API (decode_kernel.gemv,
-        the reference's operator surface): per step, the step's activations
-        come from pinned host memory and the outputs go back to the host.
+e2e     the same metric through the public Python API (decode_kernel.gemv_out,
+        the reference's operator surface writing into a preallocated output),
+        one eager call per GEMV: per step, the step's activations come from
+        pinned host memory and the outputs go back to the host.
 cpu_baseline / --impl reference
         the reference's CPU path (fp32 dequantize-then-matmul,
         python/decode_kernel/reference.py:17-26) restated in numpy
@@ -373,10 +374,14 @@ def run_ours(args) -> None:
     dx = torch.empty((S, B, K), dtype=torch.float16, device=dev)
     dy = torch.empty((S, B, M), dtype=torch.float16, device=dev)
 
+    # Eager public-API calls, one per GEMV, into the step's output buffer (no
+    # allocation per call), launched with PDL like the device-timed chain.
+    pdl = not args.no_pdl
+
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         for s in range(S):
-            dy[s].copy_(dk.gemv(packed[s], scales[s], dx[s]))
+            dk.gemv_out(packed[s], scales[s], dx[s], dy[s], pdl=pdl)
         hy.copy_(dy, non_blocking=True)
 
     for _ in range(2):
@@ -456,7 +461,8 @@ def run_ours(args) -> None:
         "e2e": {"value": e2e_value, "unit": "GB/s",
                 "h2d_bytes_per_step": S * B * K * 2, "d2h_bytes_per_step": S * B * M * 2,
                 "steps": e2e_steps,
-                "path": "decode_kernel.gemv (torch extension -> C ABI), pinned host x/y"},
+                "path": "decode_kernel.gemv_out per GEMV, eager (torch extension -> C ABI), "
+                        "PDL; one pinned-host H2D of the step's x and one D2H of its y"},
         "gpu_launches": launches,
         "clocks": clk,
     }
