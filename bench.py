@@ -592,6 +592,130 @@ def run_sharded(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def tp_layer_shapes(workload: str):
+    """(hidden, q rows, k/v rows, intermediate) of one decoder layer: Llama-2-7B
+    (MHA, 32 heads of 128) and the Llama-70B shapes (GQA: 64 query and 8 kv
+    heads of 128)."""
+    return (4096, 4096, 4096, 11008) if workload == "llama7b-tp" else (8192, 8192, 1024, 28672)
+
+
+def run_tensor_parallel(args) -> None:
+    """A decoder layer's projections in the tensor-parallel layout: q/k/v and
+    gate/up (with the SiLU-mul epilogue) split by output rows with no
+    exchange, o and down K-parallel over the same split with the fused
+    reduction -- two exchanges per layer.  Attention itself is not run: o
+    reads the rank's q slice (the shape of its heads' attention output)."""
+    import datetime
+
+    import torch
+
+    from decode_kernel.quantize import quantize_and_pack_cuda
+    from decode_kernel.sharded import (PeerBuffers, TensorParallelAttentionProj,
+                                       TensorParallelMLP, split_dim)
+
+    ws, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B = args.batch
+    layers = args.layers or (32 if args.workload == "llama7b-tp" else 8)
+    H, Q, KV, I = tp_layer_shapes(args.workload)
+    peers = PeerBuffers(4 * ws * B * H)
+
+    def mat(m, k, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)  # same weights on every rank
+        w = torch.randn(m, k, generator=g, device=dev) * 0.02
+        out = quantize_and_pack_cuda(w)
+        del w
+        return out
+
+    blocks = []
+    for layer in range(layers):
+        s0 = 9000 + 10 * layer
+        attn = TensorParallelAttentionProj(mat(Q, H, s0), mat(KV, H, s0 + 1), mat(KV, H, s0 + 2),
+                                           mat(H, Q, s0 + 3), peers, max_batch=B,
+                                           exchange=args.exchange)
+        mlp = TensorParallelMLP(mat(I, H, s0 + 4), mat(I, H, s0 + 5), mat(H, I, s0 + 6), peers,
+                                max_batch=B, exchange=args.exchange)
+        blocks.append((attn, mlp))
+        torch.cuda.empty_cache()
+    x = torch.randn(B, H, generator=torch.Generator(device=dev).manual_seed(1), device=dev).half()
+    # This rank's algorithmic bytes per layer: its weight slices, x per kernel,
+    # the local outputs, and the partials it exchanges.
+    _, nq = split_dim(Q, ws, rank)
+    _, nkv = split_dim(KV, ws, rank)
+    _, ni = split_dim(I, ws, rank)
+    per_layer = (gemv_bytes(nq + 2 * nkv, H, B) + gemv_bytes(H, nq, B) + gemv_bytes(2 * ni, H, B)
+                 - B * ni * 2 + gemv_bytes(H, ni, B))
+    if ws > 1 and args.exchange == "fused":
+        per_layer += 2 * (ws - 1) * B * H * 4
+    shard_bytes = per_layer * layers
+    pdl = not args.no_pdl and args.exchange == "fused"
+    # this library's kernels per layer: q/k/v, o (+ sum), gate/up, down (+ sum)
+    launches = layers * (4 + (2 if ws > 1 and args.exchange == "fused" else 0))
+
+    def step():
+        for attn, mlp in blocks:
+            attn(x, pdl=pdl)
+            mlp(x, pdl=pdl)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    total = torch.tensor([float(shard_bytes)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(total)
+    from decode_kernel import capi
+
+    err = capi.load().dk_device_error(-1, 0)
+    del graph
+    torch.cuda.synchronize()
+    peers.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_max = float(t[0].item())
+    value = float(total.item()) * args.steps / (ms_max / 1e3) / 1e9
+    line = {
+        "metric": f"aggregate HBM read GB/s, {args.workload} decode-step projections",
+        "value": value, "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "us_per_token": ms_max * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4*f16->f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} x{layers} layers (hidden {H}, q {Q}, k/v {KV}, "
+                               f"intermediate {I}), B={B}; attention not run",
+                   "global_batch": B, "exchange": args.exchange, "pdl": pdl,
+                   "parallelism": f"tensor-parallel x{ws}: 2 exchanges per layer",
+                   "l2": "inputs larger than L2 (the step streams every layer's weights)"},
+        "device_error": err, "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -606,9 +730,13 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["gemv", "llama7b", "llama70b"], default="gemv",
+    ap.add_argument("--workload",
+                    choices=["gemv", "llama7b", "llama70b", "llama7b-tp", "llama70b-tp"],
+                    default="gemv",
                     help="gemv: the BASELINE metric; llama7b / llama70b: the sharded model "
-                         "decode-step GEMV stacks (strong scaling over the ranks)")
+                         "decode-step GEMV stacks, every GEMV gathered (strong scaling over "
+                         "the ranks); llama7b-tp / llama70b-tp: the same layers in the "
+                         "tensor-parallel layout, two exchanges per layer")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused")
     ap.add_argument("--layers", type=int, default=0)
     args = ap.parse_args()
@@ -616,6 +744,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload.endswith("-tp"):
+        run_tensor_parallel(args)
     elif args.workload != "gemv":
         run_sharded(args)
     else:

@@ -9,6 +9,11 @@ Two layouts (the reference is single-GPU; these serve its 7B-stack and
 * ``KParallelW4A16`` -- rank r owns a group-aligned slice of K (copied once
   into its own contiguous ``packed``/``scales``); every rank computes an fp32
   partial ``[B, M]`` and every rank ends with the sum in rank order.
+* ``TensorParallelAttentionProj`` / ``TensorParallelMLP`` -- a decoder
+  layer's projections in the tensor-parallel layout: q/k/v and gate/up split
+  by output rows (heads, intermediate size) with no exchange, o and down
+  K-parallel over the same split; one exchange per block instead of one per
+  projection.
 
 ``exchange="fused"`` (default) runs the exchange inside the GEMV: the kernel's
 epilogue stores its results straight into every rank's buffer over NVLink peer
@@ -48,6 +53,9 @@ __all__ = [
     "k_range",
     "slice_rows",
     "slice_k",
+    "split_dim",
+    "TensorParallelMLP",
+    "TensorParallelAttentionProj",
 ]
 
 
@@ -369,6 +377,63 @@ class KParallelW4A16:
                    "dk_shard_reduce")
         return self.out[r0][:B]
 
+    def forward_local(self, xs: dict, pdl: bool = False) -> torch.Tensor:
+        """Like ``__call__``, but each local rank r brings only its own K
+        slice of x: ``xs[r]`` contiguous fp16 [B, kn_r] (a tensor-parallel
+        layer's local activations).  Same result as ``__call__`` on the full
+        x, bit for bit."""
+        if sorted(xs) != sorted(self.shards):
+            raise RuntimeError(f"expected inputs for ranks {sorted(self.shards)}")
+        B = None
+        for r, x in xs.items():
+            kn = self.shards[r][0].shape[1] * 8
+            if x.dtype != torch.float16 or not x.is_contiguous() or x.dim() != 2 or x.shape[1] != kn:
+                raise RuntimeError(f"rank {r}: x must be contiguous fp16 [B, {kn}]")
+            if B is not None and x.shape[0] != B:
+                raise RuntimeError("every rank's x must have the same batch")
+            B = x.shape[0]
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
+        if self.exchange == "nccl":
+            return self._nccl_local(xs[self.peers.rank])
+        lib, st = self.peers.lib, _stream()
+        r0 = next(iter(self.shards))
+        if self.peers.world == 1 and not self.peers.emulated:
+            p, s, _ = self.shards[r0]
+            _check(capi.gemv(p.data_ptr(), s.data_ptr(), xs[r0].data_ptr(),
+                             self.out[r0].data_ptr(), self.M, self.K, B, _cfg(pdl), 0, 0, st),
+                   "dk_w4a16_gemv")
+            return self.out[r0][:B]
+        inline = not self.peers.emulated
+        cfg = _cfg(pdl, await_all=inline)
+        which = self.peers.begin()
+        groups = {r: self.peers.group(r, which) for r in self.shards}
+        for r, (p, s, _) in self.shards.items():
+            kn = p.shape[1] * 8
+            _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), xs[r].data_ptr(), kn,
+                                            self.M, kn, B, ctypes.byref(groups[r]),
+                                            ctypes.byref(cfg), st), "dk_w4a16_gemv_kshard")
+        for r in self.shards:
+            _check(lib.dk_shard_reduce(ctypes.byref(groups[r]), self.M, B,
+                                       self.out[r][:B].data_ptr(), int(inline), st),
+                   "dk_shard_reduce")
+        return self.out[r0][:B]
+
+    def _nccl_local(self, xs: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        if self.peers.emulated:
+            raise RuntimeError("the NCCL exchange needs one process per rank")
+        p, s, _ = self.shards[self.peers.rank]
+        B, kn = xs.shape[0], p.shape[1] * 8
+        y32 = torch.empty((B, self.M), dtype=torch.float32, device=xs.device)
+        cfg = capi.default_config(version=5, flags=capi.DK_FLAG_F32_OUT)
+        _check(capi.gemv(p.data_ptr(), s.data_ptr(), xs.data_ptr(), y32.data_ptr(), self.M, kn,
+                         B, cfg, 0, 0, _stream()), "dk_w4a16_gemv")
+        if self.peers.world > 1:
+            dist.all_reduce(y32, group=self.group)
+        return y32.half()
+
     def _nccl(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
 
@@ -385,3 +450,127 @@ class KParallelW4A16:
         if self.peers.world > 1:
             dist.all_reduce(y32, group=self.group)
         return y32.half()
+
+
+# --------------------------------------------------------------------------
+# Tensor-parallel decoder-layer projections (one exchange per block)
+# --------------------------------------------------------------------------
+
+def split_dim(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Tensor-parallel split of an inner dimension -- attention heads of 128
+    (the quantization group) or a gated MLP's intermediate size: whole
+    128-wide blocks, balanced.  It is ``k_range``, so rank r's row-parallel
+    output slice is exactly the K slice of the next projection it owns."""
+    return k_range(n, world, rank)
+
+
+def _rows(packed: torch.Tensor, scales: torch.Tensor, r0: int, n: int, dev) -> tuple:
+    return packed[r0:r0 + n].to(dev).clone(), scales[r0:r0 + n].to(dev).clone()
+
+
+class TensorParallelMLP:
+    """Gated MLP ``down(silu(gate(x)) * up(x))`` across the ranks in the
+    tensor-parallel layout: gate and up are split by output rows and run as
+    one SiLU-mul GEMV pair per rank with no exchange (rank r's slice of h is
+    exactly the K slice of ``down`` it owns); ``down`` is K-parallel with the
+    fused reduction.  One exchange per call.  Every rank returns the same y:
+    fp16 of the rank-ordered sum of the fp32 partials of ``down`` over h's
+    slices, where h = ``gemv_silu_mul(gate, up, x)`` (row slices are
+    independent, so each rank's h slice has the unsharded bits).
+
+    ``gate``, ``up``, ``down``: ``(packed, scales)``; gate/up [I, K], down
+    [M, I], I a multiple of 128.
+    """
+
+    def __init__(self, gate, up, down, peers: PeerBuffers, max_batch: int = 1,
+                 exchange: str = "fused", group=None):
+        (pg, sg), (pu, su), (pd, sd) = gate, up, down
+        if pu.shape != pg.shape or su.shape != sg.shape:
+            raise ValueError("gate and up must have the same shape")
+        self.I, self.K = pg.shape[0], pg.shape[1] * 8
+        if pd.shape[1] * 8 != self.I:
+            raise ValueError("down's K must equal gate/up's rows")
+        self.M, self.peers, self.max_batch = pd.shape[0], peers, int(max_batch)
+        if self.I // GROUP_SIZE < peers.world:
+            raise ValueError("fewer 128-wide blocks of the intermediate size than ranks")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.gu, self.h = {}, {}
+        for r in peers.local_ranks():
+            i0, n = split_dim(self.I, peers.world, r)
+            self.gu[r] = _rows(pg, sg, i0, n, dev) + _rows(pu, su, i0, n, dev)
+            self.h[r] = torch.empty((self.max_batch, n), dtype=torch.float16, device=dev)
+        self.down = KParallelW4A16(pd, sd, peers, max_batch=max_batch, exchange=exchange,
+                                   group=group)
+
+    def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        B = x.shape[0]
+        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
+            raise RuntimeError("x must be contiguous fp16 [B, K]")
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
+        cfg, st = _cfg(pdl), _stream()
+        for r, (pg, sg, pu, su) in self.gu.items():
+            _check(capi.gemv_silu_mul(pg.data_ptr(), sg.data_ptr(), pu.data_ptr(), su.data_ptr(),
+                                      x.data_ptr(), self.h[r].data_ptr(), pg.shape[0], self.K, B,
+                                      cfg, st), "dk_w4a16_gemv_silu_mul")
+        return self.down.forward_local({r: self.h[r][:B] for r in self.gu}, pdl=pdl)
+
+
+class TensorParallelAttentionProj:
+    """An attention block's projections across the ranks, split by heads
+    (128 wide, the quantization group): q/k/v row-parallel as one
+    multi-matrix GEMV per rank with no exchange, o K-parallel over the same
+    head split with the fused reduction.  One exchange per call.
+
+    Attention itself is outside this library: ``__call__(x, attn=None)``
+    takes a callable ``attn(rank, q, k, v) -> out`` returning the rank's
+    attention output slice (fp16 [B, q rows of the rank]); without one, the
+    rank's q slice -- the same shape -- stands in for it.
+    """
+
+    def __init__(self, q, k, v, o, peers: PeerBuffers, max_batch: int = 1,
+                 exchange: str = "fused", group=None):
+        (pq, sq), (pk, sk), (pv, sv), (po, so) = q, k, v, o
+        self.K = pq.shape[1] * 8
+        if pk.shape[1] * 8 != self.K or pv.shape[1] * 8 != self.K:
+            raise ValueError("q, k, v must share K")
+        if pk.shape != pv.shape:
+            raise ValueError("k and v must have the same shape")
+        self.Q, self.KV = pq.shape[0], pk.shape[0]
+        if po.shape[1] * 8 != self.Q:
+            raise ValueError("o's K must equal q's rows")
+        self.M, self.peers, self.max_batch = po.shape[0], peers, int(max_batch)
+        if min(self.Q, self.KV) // GROUP_SIZE < peers.world:
+            raise ValueError("fewer 128-wide heads than ranks")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.qkv, self.outs = {}, {}
+        for r in peers.local_ranks():
+            q0, nq = split_dim(self.Q, peers.world, r)
+            k0, nk = split_dim(self.KV, peers.world, r)
+            self.qkv[r] = (_rows(pq, sq, q0, nq, dev), _rows(pk, sk, k0, nk, dev),
+                           _rows(pv, sv, k0, nk, dev))
+            self.outs[r] = tuple(torch.empty((self.max_batch, n), dtype=torch.float16, device=dev)
+                                 for n in (nq, nk, nk))
+        self.o = KParallelW4A16(po, so, peers, max_batch=max_batch, exchange=exchange,
+                                group=group)
+
+    def __call__(self, x: torch.Tensor, attn=None, pdl: bool = False) -> torch.Tensor:
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        B = x.shape[0]
+        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
+            raise RuntimeError("x must be contiguous fp16 [B, K]")
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
+        cfg, st = _cfg(pdl), _stream()
+        att = {}
+        for r, mats in self.qkv.items():
+            ys = self.outs[r]
+            _check(capi.gemv_multi([p.data_ptr() for p, _ in mats], [s.data_ptr() for _, s in mats],
+                                   [p.shape[0] for p, _ in mats], [y.data_ptr() for y in ys],
+                                   x.data_ptr(), self.K, B, cfg, st), "dk_w4a16_gemv_multi")
+            q, k, v = (y[:B] for y in ys)
+            att[r] = q if attn is None else attn(r, q, k, v)
+        return self.o.forward_local(att, pdl=pdl)

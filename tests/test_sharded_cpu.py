@@ -188,3 +188,66 @@ def test_f32_flag_only_on_the_streaming_kernel():
         assert capi.gemv(16, 16, 16, 16, 64, 256, 1, c) == capi.DK_ERR_UNSUPPORTED
     assert capi.gemv(16, 16, 16, 16, 64, 256, 1,
                      capi.default_config(flags=0x8)) == capi.DK_ERR_INVALID_ARG
+
+
+def _tp_rank_main(rank: int, world: int, port: int, out_path: str) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from decode_kernel.sharded import split_dim
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        (pg, sg, x), (pu, su, _), (pd, sd, _) = _tp_problem()
+        # gate/up: this rank's output rows; down: the same range of its K
+        i0, n = split_dim(pg.shape[0], world, rank)
+        g = O.linear_fp32(x, pg[i0:i0 + n], sg[i0:i0 + n]).astype(np.float64)
+        u = O.linear_fp32(x, pu[i0:i0 + n], su[i0:i0 + n]).astype(np.float64)
+        h = (g / (1 + np.exp(-g)) * u).astype(np.float16)
+        p = np.ascontiguousarray(pd[:, i0 // 8:(i0 + n) // 8])
+        s = np.ascontiguousarray(sd[:, i0 // 128:(i0 + n) // 128])
+        part = torch.from_numpy(O.linear_fp32(h, p, s))
+        dist.all_reduce(part)  # the block's one exchange
+        np.save(f"{out_path}.{rank}.npy", part.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _tp_problem():
+    I, K, M, B = 640, 256, 64, 2  # 5 blocks of 128: unequal splits at 2 and 3 ranks
+    return (make_problem(I, K, B, seed=95), make_problem(I, K, 1, seed=96),
+            make_problem(M, I, 1, seed=97))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_tensor_parallel_mlp_matches_whole_layer(world, tmp_path):
+    # The row split of gate/up is the K split of down, so the ranks' partials
+    # of down over their own h slices add up to the whole layer.
+    import torch.multiprocessing as mp
+
+    from oracle import oracle as O
+
+    out = str(tmp_path / "y")
+    mp.start_processes(_tp_rank_main, args=(world, _free_port(), out), nprocs=world,
+                       start_method="spawn", join=True)
+    (pg, sg, x), (pu, su, _), (pd, sd, _) = _tp_problem()
+    g = O.linear_fp32(x, pg, sg).astype(np.float64)
+    u = O.linear_fp32(x, pu, su).astype(np.float64)
+    h = (g / (1 + np.exp(-g)) * u).astype(np.float16)
+    ref = O.linear_fp32(h, pd, sd)
+    for r in range(world):
+        y = np.load(f"{out}.{r}.npy")
+        assert y.shape == ref.shape
+        assert np.abs(y - ref).max() < 1e-4 * max(1.0, np.abs(ref).max())
+
+
+def test_split_dim_is_head_aligned():
+    from decode_kernel.sharded import k_range, split_dim
+
+    for n, world in [(8192, 8), (1024, 8), (11008, 4), (28672, 8)]:
+        parts = [split_dim(n, world, r) for r in range(world)]
+        assert parts == [k_range(n, world, r) for r in range(world)]
+        assert all(k0 % 128 == 0 and kn % 128 == 0 and kn > 0 for k0, kn in parts)
+        assert sum(kn for _, kn in parts) == n

@@ -181,6 +181,73 @@ def test_row_parallel_step_replays_from_a_cuda_graph(cuda_device):
         peers.close()
 
 
+def _k_parallel_expected(pd, sd, h, world):
+    """fp16 of the rank-ordered sum of the fp32 GEMVs of down's K slices."""
+    from decode_kernel.sharded import slice_k
+
+    acc = torch.zeros((h.shape[0], pd.shape[0]), dtype=torch.float32, device=h.device)
+    for r in range(world):
+        p, s, k0 = slice_k(pd, sd, world, r)
+        acc += f32_gemv(p, s, h[:, k0:k0 + p.shape[1] * 8].contiguous())
+    return acc.half()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4])
+@pytest.mark.parametrize("B", [1, 3])
+def test_tensor_parallel_mlp_emulated(world, B, cuda_device):
+    # gate/up row-parallel through the SiLU-mul pair, down K-parallel over the
+    # same split (9 blocks of 128: unequal for 2 and 4 ranks).
+    from decode_kernel import gemv_silu_mul
+    from decode_kernel.sharded import PeerBuffers, TensorParallelMLP
+
+    I, K, M = 1152, 512, 384
+    pg, sg, x = make_problem(I, K, B, seed=500 + world, std=0.05)
+    pu, su, _ = make_problem(I, K, 1, seed=600 + world, std=0.05)
+    pd, sd, _ = make_problem(M, I, 1, seed=700 + world, std=0.05)
+    (tg, tsg, tx), (tu, tsu, _), (td, tsd, _) = (to_device(pg, sg, x), to_device(pu, su, x),
+                                                  to_device(pd, sd, x[:, :0]))
+    peers = PeerBuffers(4 * world * B * M, emulate=world)
+    mlp = TensorParallelMLP((tg, tsg), (tu, tsu), (td, tsd), peers, max_batch=B)
+    try:
+        for call in range(2):
+            xc = (tx * (1 + call)).contiguous()
+            y = mlp(xc, pdl=(call == 1)).clone()
+            h = gemv_silu_mul((tg, tsg), (tu, tsu), xc)
+            assert torch.equal(y, _k_parallel_expected(td, tsd, h, world)), call
+        from decode_kernel import capi
+
+        assert capi.load().dk_device_error(-1, 1) == 0
+    finally:
+        peers.close()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_tensor_parallel_attention_proj_emulated(world, cuda_device):
+    # q/k/v by heads in one multi-GEMV per rank, o K-parallel over the head
+    # split; the rank's q slice stands in for its attention output.
+    from decode_kernel.sharded import PeerBuffers, TensorParallelAttentionProj
+
+    B, K, Q, KV = 2, 1024, 1024, 512
+    mats = [make_problem(m, K, B, seed=800 + i, std=0.05) for i, m in enumerate((Q, KV, KV))]
+    po, so, _ = make_problem(K, Q, 1, seed=900, std=0.05)
+    x = mats[0][2]
+    dq, dk_, dv = (to_device(p, s, x) for p, s, _ in mats)
+    tx = dq[2]
+    to, tso, _ = to_device(po, so, x[:, :0])
+    peers = PeerBuffers(4 * world * B * K, emulate=world)
+    proj = TensorParallelAttentionProj(dq[:2], dk_[:2], dv[:2], (to, tso), peers, max_batch=B)
+    try:
+        y = proj(tx).clone()
+        q = capi_gemv(*dq[:2], tx)
+        assert torch.equal(y, _k_parallel_expected(to, tso, q, world))
+        seen = []
+        proj(tx, attn=lambda r, q_, k_, v_: seen.append((r, q_.shape, k_.shape, v_.shape)) or q_)
+        assert [r for r, *_ in seen] == list(range(world))
+        assert sum(sh[1][1] for sh in seen) == Q and sum(sh[2][1] for sh in seen) == KV
+    finally:
+        peers.close()
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -205,20 +272,35 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         tp = torch.from_numpy(packed).to(dev)
         ts = torch.from_numpy(scales.view(np.int16)).to(dev).view(torch.float16)
         tx = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.float16)
-        peers = PeerBuffers(4 * world * B * M)
+        peers = PeerBuffers(4 * world * B * max(M, K))
         rowl = RowParallelW4A16(tp, ts, peers, max_batch=B)
         kl = KParallelW4A16(tp, ts, peers, max_batch=B)
         y_row = rowl(tx).clone()
         y_k = kl(tx).clone()
         y_row_nccl = RowParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
         y_k_nccl = KParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
+        # Tensor-parallel MLP (gate/up = W, down = W's first K rows as [K, M]
+        # shapes): real ranks, NCCL, and both ranks emulated on this GPU.
+        from decode_kernel.sharded import TensorParallelMLP
+
+        pd, sd, _ = make_problem(K, M, 1, seed=78)
+        td = torch.from_numpy(pd).to(dev)
+        tsd = torch.from_numpy(sd.view(np.int16)).to(dev).view(torch.float16)
+        args = ((tp, ts), (tp, ts), (td, tsd))
+        y_tp = TensorParallelMLP(*args, peers, max_batch=B)(tx).clone()
+        y_tp_nccl = TensorParallelMLP(*args, peers, max_batch=B, exchange="nccl")(tx).clone()
+        emu = PeerBuffers(4 * world * B * K, emulate=world)
+        y_tp_emu = TensorParallelMLP(*args, emu, max_batch=B)(tx).clone()
         torch.cuda.synchronize()
+        emu.close()
         from decode_kernel import capi
 
         err = capi.load().dk_device_error(-1, 0)
         np.savez(f"{out_path}.{rank}.npz", row=y_row.float().cpu().numpy(),
                  k=y_k.float().cpu().numpy(), row_nccl=y_row_nccl.float().cpu().numpy(),
-                 k_nccl=y_k_nccl.float().cpu().numpy(), err=err)
+                 k_nccl=y_k_nccl.float().cpu().numpy(), tp=y_tp.float().cpu().numpy(),
+                 tp_nccl=y_tp_nccl.float().cpu().numpy(), tp_emu=y_tp_emu.float().cpu().numpy(),
+                 err=err)
         dist.barrier()
         peers.close()
     finally:
@@ -246,5 +328,9 @@ def test_two_real_ranks_fused_and_nccl(tmp_path):
         assert int(g["err"]) == 0
         assert np.array_equal(g["row"], got[0]["row"]) and np.array_equal(g["k"], got[0]["k"])
         assert np.array_equal(g["row"], g["row_nccl"])  # same kernel rows, gathered
+        # the fused exchange sums the two partials as NCCL does (a + b), and the
+        # real ranks equal the emulated ones bit for bit
+        assert np.array_equal(g["tp"], g["tp_emu"]) and np.array_equal(g["tp"], g["tp_nccl"])
+        assert np.array_equal(g["tp"], got[0]["tp"])
         for key in ("row", "k", "row_nccl", "k_nccl"):
             assert np.abs(g[key] - ref).max() < MAX_ABS, key
