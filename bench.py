@@ -510,7 +510,7 @@ def run_sharded(args) -> None:
     layers = args.layers or (32 if args.workload == "llama7b" else 8)
     shapes = model_gemvs(args.workload, layers)
     maxm = max(m for m, _, _ in shapes)
-    peers = PeerBuffers(max(2 * B * maxm, 4 * ws * B * maxm))
+    peers = PeerBuffers(max(2 * B * maxm, 8 * ws * B * maxm))
     xs = {}
     mods, shard_bytes = [], 0
     for i, (M, K, layout) in enumerate(shapes):
@@ -624,7 +624,7 @@ def run_tensor_parallel(args) -> None:
     B = args.batch
     layers = args.layers or (32 if args.workload == "llama7b-tp" else 8)
     H, Q, KV, I = tp_layer_shapes(args.workload)
-    peers = PeerBuffers(4 * ws * B * H)
+    peers = PeerBuffers(8 * ws * B * H)
 
     def mat(m, k, seed):
         g = torch.Generator(device=dev).manual_seed(seed)  # same weights on every rank

@@ -255,6 +255,20 @@ __device__ __forceinline__ unsigned ld_relaxed_sys_u32(const unsigned* p) {
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Low-latency exchange words: a value and the call's sequence number in one
+// naturally aligned 64-bit word, stored and loaded as single 64-bit accesses
+// (single-copy atomic, also across NVLink), so a reader that sees the number
+// sees the value with it -- no fence between data and flag.
+__device__ __forceinline__ void st_ll_sys(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll_sys(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
 __device__ inline bool wait_slots(const unsigned* slots, int stride, int world, int grid,
                                   unsigned epoch, int* err) {
   const int lane = threadIdx.x & 31;

@@ -55,7 +55,8 @@ enum OutMode : int {
   kOutHalf = 0,      // fp16 y [B, M]
   kOutFloat = 1,     // fp32 dst[0] [B, M]
   kOutRowShard = 2,  // fp16 into every rank's dst[g] [B, ld] at columns col0 + m
-  kOutKShard = 3,    // fp32 partial into every rank's dst[g] [world][B][M], slot `rank`
+  kOutKShard = 3,    // fp32 partial into every rank's dst[g] [world][B][M], slot `rank`, as
+                     // 64-bit {value, call number} words (low-latency exchange)
 };
 constexpr int kMaxShards = DK_MAX_SHARDS;
 struct OutSpec {
@@ -173,8 +174,10 @@ struct CtaTiles {
   }
 };
 
-// v5 result store for batch row b, output row m.
-__device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v) {
+// v5 result store for batch row b, output row m.  `tag`: the call's sequence
+// number (K-shard mode only).
+__device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v,
+                                        unsigned tag = 0) {
   switch (p.out.mode) {
     case kOutFloat:
       static_cast<float*>(p.out.dst[0])[(size_t)b * p.M + m] = v;
@@ -187,7 +190,9 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
     }
     case kOutKShard:
       for (int g = 0; g < p.out.world; ++g)
-        static_cast<float*>(p.out.dst[g])[((size_t)p.out.rank * p.B + b) * p.M + m] = v;
+        st_ll_sys(static_cast<unsigned long long*>(p.out.dst[g]) +
+                      ((size_t)p.out.rank * p.B + b) * p.M + m,
+                  v, tag);
       break;
     default:
       p.y[(size_t)b * p.M + m] = __float2half_rn(v);
@@ -202,7 +207,7 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
 // with the gather complete while a PDL-launched successor already streams
 // its weights.  Called by the one warp that wrote y, all lanes.
 __device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
-  if (p.out.mode < kOutRowShard) return;
+  if (p.out.mode != kOutRowShard) return;  // K-shard words carry their own call number
   pdl_wait();  // seq was advanced by the previous sharded call
   const unsigned epoch = *reinterpret_cast<volatile unsigned*>(p.out.seq) + 1;
   __syncwarp();
@@ -866,6 +871,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     StageCursor cur;
     int issued = 0, reduced = 0;
     uint64_t idle_since = 0;
+    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
     while (issued < total || reduced < ntiles) {
       bool progress = false;
       if (issued < total) {
@@ -937,6 +943,10 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
         const TileRef tr = tiles(a, reduced);
         const int trow = tr.row, rows = tr.rows;
         const int nb = min(W, p.B);
+        if (!MULTI && reduced == 0 && p.out.mode == kOutKShard) {
+          pdl_wait();  // the number was advanced by the previous call's sum
+          tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+        }
         constexpr bool paired = SEG == kSegPair;
         if (paired && tr.seg == 0) {
           // Gate tile: its partials stay in their buffer until the up tile
@@ -969,7 +979,7 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
                 sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
               }
             } else {
-              store_y(p, b, trow + r, sum);
+              store_y(p, b, trow + r, sum, tag);
             }
           }
           __syncwarp();
@@ -1705,13 +1715,16 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   dk_status s = validate_config(c);
   if (s != DK_OK) return s;
   if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
-  const bool await_all = (c.flags & DK_FLAG_SHARD_WAIT) != 0;
+  const bool kshard = p.out.mode == kOutKShard;
+  const bool await_all = (c.flags & DK_FLAG_SHARD_WAIT) != 0 && !kshard;
   if (sm_count(-1) > DK_SHARD_SLOTS) return DK_ERR_UNSUPPORTED;
   if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
       !g->seq)
     return DK_ERR_INVALID_ARG;
   for (int i = 0; i < g->world; ++i)
-    if (!g->bufs[i] || !g->slots[i]) return DK_ERR_INVALID_ARG;
+    if (!g->bufs[i] || (!kshard && !g->slots[i]) ||
+        (kshard && (reinterpret_cast<uintptr_t>(g->bufs[i]) & 7u)))
+      return DK_ERR_INVALID_ARG;
   if (p.M <= 0 || p.K <= 0 || p.K % DK_GROUP_SIZE != 0 || p.B <= 0) return DK_ERR_INVALID_ARG;
   if (p.B > kMaxBatchPerPass) return DK_ERR_UNSUPPORTED;
   if (!p.packed || !p.scales || !p.x || !aligned16(p.packed) || !aligned16(p.x) ||

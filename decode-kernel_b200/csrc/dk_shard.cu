@@ -4,12 +4,17 @@
 // number lives on the device (dk_shard_group::seq), so a captured CUDA graph
 // of sharded calls replays correctly.
 //
-// The GEMV kernels themselves (dk_w4a16_gemv_rowshard / _kshard in
-// dk_gemv.cu) store their results into every rank's buffer and then, per CTA,
-// release-store the call's sequence number into that CTA's slot of every
-// rank's slot array.  The waits read the local slots with acquire semantics
-// at system scope, so everything the ranks stored before marking their slots
-// is visible to the work that follows on the stream.
+// Row-parallel (dk_w4a16_gemv_rowshard in dk_gemv.cu): the kernel stores its
+// rows into every rank's buffer and then, per CTA, release-stores the call's
+// sequence number into that CTA's slot of every rank's slot array.  The waits
+// read the local slots with acquire semantics at system scope, so everything
+// the ranks stored before marking their slots is visible to the work that
+// follows on the stream.
+//
+// K-parallel (dk_w4a16_gemv_kshard): the low-latency exchange.  Every fp32
+// partial travels with the call's sequence number in one 64-bit word, so the
+// sum polls the words themselves -- no release fence on the writer, no slot
+// handshake, no separate wait.
 #include <cstring>
 
 #include "dk_device.cuh"
@@ -27,13 +32,43 @@ __global__ void k_shard_wait(const unsigned* slots, unsigned* seq, int world, in
   if (threadIdx.x == 0) seq[0] = epoch;
 }
 
-// y[i] = fp16(sum_r part[r][i]) in ascending r; part is [world][n].  The
-// partials were stored by other GPUs: read them from L2.
-__global__ void k_shard_sum(const float* part, int world, int n, __half* y) {
+// y[i] = fp16(sum_r part[r][i]) in ascending r; part is [world][n] of 64-bit
+// {value, call number} words stored by every rank's GEMV (this GPU's own
+// included).  Each word is polled until it carries this call's number
+// (bounded: the clock is checked every 256 polls); the last block to finish
+// advances seq[0], which every block read before counting itself done
+// (seq[2] counts the blocks).
+__global__ void k_shard_sum(const unsigned long long* part, int world, int n, __half* y,
+                            unsigned* seq, int* err) {
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(seq) + 1;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) s_abort = 0;
+  __syncthreads();
+  const uint64_t t0 = globaltimer_ns();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float s = 0.f;
-    for (int r = 0; r < world; ++r) s = __fadd_rn(s, __ldcg(part + (size_t)r * n + i));
+    for (int r = 0; r < world; ++r) {
+      unsigned long long w = ld_ll_sys(part + (size_t)r * n + i);
+      for (unsigned polls = 1; (unsigned)(w >> 32) != epoch; ++polls) {
+        if ((polls & 255u) == 0 &&
+            (*reinterpret_cast<volatile int*>(&s_abort) || globaltimer_ns() - t0 > kWaitLimitNs)) {
+          if (!s_abort) atomicExch(err, kDevWaitTimeout);
+          s_abort = 1;
+          break;
+        }
+        w = ld_ll_sys(part + (size_t)r * n + i);
+      }
+      s = __fadd_rn(s, __uint_as_float((unsigned)w));
+    }
     y[i] = __float2half_rn(s);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(seq + 2, 1u) == gridDim.x - 1) {
+      seq[2] = 0;
+      seq[0] = epoch;
+    }
   }
 }
 
@@ -60,15 +95,18 @@ extern "C" dk_status dk_shard_reduce(const dk_shard_group* group, int M, int B, 
                                      int waited, void* stream) {
   if (!group_ok(group) || !group->bufs[group->rank] || !y || M < 0 || B < 0)
     return DK_ERR_INVALID_ARG;
+  (void)waited;  // the words carry their call number: nothing to wait for first
   const long long n = (long long)M * B;
   if (n > (1ll << 30)) return DK_ERR_UNSUPPORTED;
-  dk_status s = waited ? DK_OK : dk_shard_wait(group, stream);
-  if (s != DK_OK || n == 0) return s;
+  if (n == 0) return DK_OK;
+  if (reinterpret_cast<uintptr_t>(group->bufs[group->rank]) & 7u) return DK_ERR_INVALID_ARG;
+  int* err = device_error_address();
+  if (!err) return DK_ERR_CUDA;
   const int threads = 256;
   const int blocks = (int)std::min<long long>((n + threads - 1) / threads, 4ll * sm_count(-1));
   k_shard_sum<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const float*>(group->bufs[group->rank]), group->world, (int)n,
-      reinterpret_cast<__half*>(y));
+      static_cast<const unsigned long long*>(group->bufs[group->rank]), group->world, (int)n,
+      reinterpret_cast<__half*>(y), group->seq, err);
   return check_launch("k_shard_sum");
 }
 

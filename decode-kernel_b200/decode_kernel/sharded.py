@@ -8,7 +8,9 @@ Two layouts (the reference is single-GPU; these serve its 7B-stack and
   no repacking); ``x`` is replicated; every rank ends with the full ``y``.
 * ``KParallelW4A16`` -- rank r owns a group-aligned slice of K (copied once
   into its own contiguous ``packed``/``scales``); every rank computes an fp32
-  partial ``[B, M]`` and every rank ends with the sum in rank order.
+  partial ``[B, M]`` and every rank ends with the sum in rank order.  The
+  partials travel as 64-bit {value, call number} words (8 bytes per value
+  in the peer buffers), which the sum polls directly.
 * ``TensorParallelAttentionProj`` / ``TensorParallelMLP`` -- a decoder
   layer's projections in the tensor-parallel layout: q/k/v and gate/up split
   by output rows (heads, intermediate size) with no exchange, o and down
@@ -335,8 +337,8 @@ class KParallelW4A16:
         self.M, self.K = packed.shape[0], packed.shape[1] * 8
         self.peers, self.exchange, self.group = peers, exchange, group
         self.max_batch = int(max_batch)
-        if 4 * peers.world * self.max_batch * self.M > peers.nbytes:
-            raise ValueError("peer buffers too small for [world, max_batch, M] fp32")
+        if 8 * peers.world * self.max_batch * self.M > peers.nbytes:
+            raise ValueError("peer buffers too small for [world, max_batch, M] 64-bit words")
         dev = torch.device("cuda", torch.cuda.current_device())
         self.shards = {}
         for r in peers.local_ranks():

@@ -173,11 +173,14 @@ DK_API dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate, const uint16
  * row-parallel (output rows split, results all-gathered) and K-parallel
  * (reduction split, partials summed) layouts, with the exchange fused into
  * the GEMV: every CTA stores its results straight into every rank's buffer
- * over NVLink peer memory and then, with one release store per rank, marks
- * its arrival slot in every rank's slot array with the call's sequence
- * number.  A rank may read the gathered result once all world * grid slots
- * of its own array carry that number.  All ranks must run on the same GPU
- * model (the grid is derived from the shape and the SM count).
+ * over NVLink peer memory.  Row-parallel: each CTA then marks its arrival
+ * slot in every rank's slot array with the call's sequence number (one
+ * release store per rank), and a rank may read the gathered result once all
+ * world * grid slots of its own array carry that number.  K-parallel: each
+ * partial travels with the call's sequence number in one 64-bit word, and
+ * the sum polls the words themselves (no slots, no separate wait).  All
+ * ranks must run on the same GPU model (the grid is derived from the shape
+ * and the SM count).
  * ------------------------------------------------------------------------ */
 #define DK_MAX_SHARDS 8
 #define DK_SHARD_SLOTS 256 /* arrival slots per rank and call, >= any grid */
@@ -188,11 +191,13 @@ typedef struct dk_shard_group {
   unsigned* slots[DK_MAX_SHARDS];  /* every rank's arrival slots, mapped here:
                                     * unsigned [DK_MAX_SHARDS][DK_SHARD_SLOTS],
                                     * zero before the first call */
-  unsigned* seq;                   /* this rank's own unsigned[2] in device
+  unsigned* seq;                   /* this rank's own unsigned[4] in device
                                     * memory, zero before the first call:
                                     * [0] sharded calls completed on this group,
-                                    * [1] CTAs per rank of the last call.  Kept
-                                    * on the device so captured graphs replay. */
+                                    * [1] CTAs per rank of the last row-parallel
+                                    * call, [2] blocks of the running K-parallel
+                                    * sum done.  Kept on the device so captured
+                                    * graphs replay. */
 } dk_shard_group;
 
 /* Row-parallel shard: this rank holds rows [row0, row0 + M_shard) of an
@@ -208,8 +213,11 @@ DK_API dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_t* s
 /* K-parallel shard: this rank holds a group-aligned K slice of an [M, K]
  * weight as its own contiguous packed [M, K_shard/8] and scales
  * [M, K_shard/128]; x points at the slice's first column of the full fp16 x,
- * whose rows are ldx elements apart.  Every rank's bufs[g] is fp32
- * [world][B][M]; this call writes slot `rank` of all of them.  B <= 32. */
+ * whose rows are ldx elements apart.  Every rank's bufs[g] (8-byte aligned)
+ * holds [world][B][M] 64-bit words {fp32 partial in the low half, the call's
+ * sequence number seq[0] + 1 in the high half}; this call writes slot `rank`
+ * of all of them.  DK_FLAG_SHARD_WAIT is ignored (nothing to wait for).
+ * B <= 32. */
 DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* scales,
                                       const uint16_t* x, int ldx, int M, int K_shard, int B,
                                       const dk_shard_group* group, const dk_gemv_config* cfg,
@@ -221,11 +229,11 @@ DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* sca
  * 2 s it records the timeout in dk_device_error and lets the stream go on. */
 DK_API dk_status dk_shard_wait(const dk_shard_group* group, void* stream);
 
-/* K-parallel finish: the wait above (skipped when `waited` is non-zero, i.e.
- * the GEMV ran with DK_FLAG_SHARD_WAIT), then y[b, m] = fp16(sum over
- * r = 0..world-1, in that order, of partials[r][b][m]) with partials = this
- * rank's buffer bufs[rank] (fp32 [world][B][M]).  Every rank computes the
- * same bits. */
+/* K-parallel finish: y[b, m] = fp16(sum over r = 0..world-1, in that order,
+ * of partials[r][b][m]) with partials = this rank's buffer bufs[rank] (the
+ * 64-bit words above).  Each word is polled until it carries this call's
+ * number, then seq[0] += 1; bounded like dk_shard_wait.  `waited` is kept for
+ * compatibility and ignored.  Every rank computes the same bits. */
 DK_API dk_status dk_shard_reduce(const dk_shard_group* group, int M, int B, uint16_t* y,
                                  int waited, void* stream);
 

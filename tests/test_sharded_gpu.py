@@ -88,7 +88,7 @@ def test_k_parallel_emulated_sums_the_slices_in_rank_order(world, B, cuda_device
     M, K = 512, 11008  # 86 groups: unequal slices for 4 and 8 ranks
     packed, scales, x = make_problem(M, K, B, seed=300 + world, std=0.05)
     tp, ts, tx = to_device(packed, scales, x)
-    peers = PeerBuffers(4 * world * B * M, emulate=world)
+    peers = PeerBuffers(8 * world * B * M, emulate=world)
     layer = KParallelW4A16(tp, ts, peers, max_batch=B)
     try:
         for call in range(2):
@@ -206,7 +206,7 @@ def test_tensor_parallel_mlp_emulated(world, B, cuda_device):
     pd, sd, _ = make_problem(M, I, 1, seed=700 + world, std=0.05)
     (tg, tsg, tx), (tu, tsu, _), (td, tsd, _) = (to_device(pg, sg, x), to_device(pu, su, x),
                                                   to_device(pd, sd, x[:, :0]))
-    peers = PeerBuffers(4 * world * B * M, emulate=world)
+    peers = PeerBuffers(8 * world * B * M, emulate=world)
     mlp = TensorParallelMLP((tg, tsg), (tu, tsu), (td, tsd), peers, max_batch=B)
     try:
         for call in range(2):
@@ -234,7 +234,7 @@ def test_tensor_parallel_attention_proj_emulated(world, cuda_device):
     dq, dk_, dv = (to_device(p, s, x) for p, s, _ in mats)
     tx = dq[2]
     to, tso, _ = to_device(po, so, x[:, :0])
-    peers = PeerBuffers(4 * world * B * K, emulate=world)
+    peers = PeerBuffers(8 * world * B * K, emulate=world)
     proj = TensorParallelAttentionProj(dq[:2], dk_[:2], dv[:2], (to, tso), peers, max_batch=B)
     try:
         y = proj(tx).clone()
@@ -272,7 +272,7 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         tp = torch.from_numpy(packed).to(dev)
         ts = torch.from_numpy(scales.view(np.int16)).to(dev).view(torch.float16)
         tx = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.float16)
-        peers = PeerBuffers(4 * world * B * max(M, K))
+        peers = PeerBuffers(8 * world * B * max(M, K))
         rowl = RowParallelW4A16(tp, ts, peers, max_batch=B)
         kl = KParallelW4A16(tp, ts, peers, max_batch=B)
         y_row = rowl(tx).clone()
@@ -289,7 +289,7 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         args = ((tp, ts), (tp, ts), (td, tsd))
         y_tp = TensorParallelMLP(*args, peers, max_batch=B)(tx).clone()
         y_tp_nccl = TensorParallelMLP(*args, peers, max_batch=B, exchange="nccl")(tx).clone()
-        emu = PeerBuffers(4 * world * B * K, emulate=world)
+        emu = PeerBuffers(8 * world * B * K, emulate=world)
         y_tp_emu = TensorParallelMLP(*args, emu, max_batch=B)(tx).clone()
         torch.cuda.synchronize()
         emu.close()
