@@ -16,8 +16,10 @@ value   device-resident throughput: the step is captured once in a CUDA
         tail) and replayed K times between CUDA events.
 e2e     the same metric through the public Python API (decode_kernel.gemv_out,
         the reference's operator surface writing into a preallocated output),
-        one eager call per GEMV: per step, the step's activations come from
-        pinned host memory and the outputs go back to the host.
+        one call per GEMV, captured once with torch.cuda.graph and replayed:
+        per step, the step's activations come from pinned host memory and the
+        outputs go back to the host.  e2e.eager is the same with the calls
+        launched eagerly from Python (host-bound: ~7 µs per call).
 cpu_baseline / --impl reference
         the reference's CPU path (fp32 dequantize-then-matmul,
         python/decode_kernel/reference.py:17-26) restated in numpy
@@ -211,6 +213,76 @@ def time_cpu_reference(M, K, B, budget_s, seed=0):
     return gemv_bytes(M, K, B) / t / 1e9, t, M, n
 
 
+FLUSH_BYTES = 512 << 20  # the L2 flush of the BASELINE protocol
+
+
+def time_isolated(torch, call, iters=200, warmup=20) -> float:
+    """The reference's own timing protocol (bench/common.py:64-108 of the
+    reference, with BASELINE's 512 MiB flush): fill a 512 MiB buffer, record
+    an event, make one call, record an event, synchronize; median µs."""
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for i in range(warmup + iters):
+        flush.fill_(1.0)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= warmup:
+            ts.append(e0.elapsed_time(e1) * 1e3)
+    del flush
+    return statistics.median(ts)
+
+
+def time_reference_cuda(M, K, B, sets=64, chain_steps=20):
+    """The reference's own CUDA kernels on this GPU: csrc/gemv_w4a16.cu of the
+    reference, compiled unmodified for sm_100a (oracle/_ref, built from the
+    checkout by oracle/Makefile), called through its host entry point
+    w4a16_gemv (gemv_w4a16.cu:568-591: stamp reset copy + launch).  Its best
+    kernel (v1) and its default (v5), each (a) isolated under the reference's
+    protocol and (b) over the same 64-matrix chain as this library's
+    ``value``, launched back to back.  None when there is no GPU or the
+    reference was not built."""
+    import torch
+
+    from oracle import ref_cuda
+
+    if not torch.cuda.is_available() or not ref_cuda.available():
+        return None
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    # Timing inputs only: random packed words and small positive scales.
+    packed = [torch.randint(-2**31, 2**31 - 1, (M, K // 8), generator=g, device=dev,
+                            dtype=torch.int32) for _ in range(sets)]
+    scales = [(torch.rand(M, K // 128, generator=g, device=dev) * 0.01).half()
+              for _ in range(sets)]
+    x = torch.randn(B, K, generator=g, device=dev).half()
+    y = torch.empty(B, M, dtype=torch.float16, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {"build": "reference csrc/gemv_w4a16.cu, unmodified, nvcc -O3 --use_fast_math "
+                    "for sm_100a (its setup.py flags)",
+           "per_gemv_bytes": gemv_bytes(M, K, B)}
+    for name, ver in (("v1", 1), ("v5", 5)):
+        iso = time_isolated(torch, lambda: ref_cuda.gemv(packed[0], scales[0], x, y, version=ver))
+        for _ in range(3):
+            for s in range(sets):
+                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(chain_steps):
+            for s in range(sets):
+                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver)
+        e1.record()
+        torch.cuda.synchronize()
+        chain = e0.elapsed_time(e1) * 1e3 / (chain_steps * sets)
+        out[name] = {"isolated_us": iso, "isolated_GBps": gemv_bytes(M, K, B) / iso / 1e3,
+                     "chain_us_per_gemv": chain, "chain_GBps": gemv_bytes(M, K, B) / chain / 1e3}
+    del packed, scales
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args) -> None:
     ws, rank, _ = dist_info()
     if rank != 0:
@@ -259,6 +331,10 @@ def run_reference(args) -> None:
                       f"reference.py:17-26), {cores} BLAS threads"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_reference_cuda:
+        rc = time_reference_cuda(M, K, B)
+        if rc is not None:
+            line["reference_cuda_same_gpu"] = rc
     print(json.dumps(line), flush=True)
 
 
@@ -384,23 +460,61 @@ def run_ours(args) -> None:
             dk.gemv_out(packed[s], scales[s], dx[s], dy[s], pdl=pdl)
         hy.copy_(dy, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if pg:
-        pg.all_reduce(e2e_ms, op=pg.ReduceOp.MAX)
-    e2e_value = ws * e2e_steps * S * per_gemv / (float(e2e_ms.item()) / 1e3) / 1e9
+    # The same public-API calls captured once in a CUDA graph (how a decode
+    # loop runs them), replayed per step between the host copies.
+    gemv_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gemv_graph):
+        for s in range(S):
+            dk.gemv_out(packed[s], scales[s], dx[s], dy[s], pdl=pdl)
+
+    def e2e_graph_step():
+        dx.copy_(hx, non_blocking=True)
+        gemv_graph.replay()
+        hy.copy_(dy, non_blocking=True)
+
+    def time_e2e(fn) -> float:
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(e2e_steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return ws * e2e_steps * S * per_gemv / (float(t.item()) / 1e3) / 1e9
+
+    e2e_eager = time_e2e(e2e_step)
+    eager_y = hy.clone()
+    e2e_value = time_e2e(e2e_graph_step)
+    # The replayed calls return the eager calls' bits.
+    assert torch.equal(hy, eager_y), "graph-replayed e2e outputs differ from the eager calls"
+    del gemv_graph
 
     roof = read_roof_gbs(torch, capi) if rank == 0 else None
+
+    # One call at a time under the reference's own protocol (512 MiB flush,
+    # events around a single plain launch): the number the reference's
+    # published table is made of.
+    isolated = None
+    if rank == 0 and not args.no_isolated:
+        cfg_plain = capi.default_config()
+
+        def one_call():
+            capi.check(capi.gemv(packed[0].data_ptr(), scales[0].data_ptr(), xs[0].data_ptr(),
+                                 ys[0].data_ptr(), M, K, B, cfg_plain, 0, 0,
+                                 torch.cuda.current_stream().cuda_stream), "dk_w4a16_gemv")
+
+        iso_us = time_isolated(torch, one_call)
+        isolated = {"us_per_gemv": iso_us, "GBps": per_gemv / iso_us / 1e3,
+                    "protocol": "512 MiB fill flush, CUDA events around one C-ABI call "
+                                "(no PDL), median of 200 after 20 warm-up "
+                                "(reference bench/common.py:64-108)"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -461,11 +575,16 @@ def run_ours(args) -> None:
         "e2e": {"value": e2e_value, "unit": "GB/s",
                 "h2d_bytes_per_step": S * B * K * 2, "d2h_bytes_per_step": S * B * M * 2,
                 "steps": e2e_steps,
-                "path": "decode_kernel.gemv_out per GEMV, eager (torch extension -> C ABI), "
-                        "PDL; one pinned-host H2D of the step's x and one D2H of its y"},
+                "path": "decode_kernel.gemv_out per GEMV (torch extension -> C ABI, PDL), "
+                        "the step's calls captured once with torch.cuda.graph and replayed; "
+                        "every step: one pinned-host H2D of its x, the replay, one D2H of its y",
+                "eager": {"value": e2e_eager, "unit": "GB/s",
+                          "path": "the same calls launched eagerly, one Python call per GEMV"}},
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if isolated is not None:
+        line["isolated"] = isolated
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -730,6 +849,10 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-cuda", action="store_true",
+                    help="reference arm: skip timing the reference's own CUDA kernels")
+    ap.add_argument("--no-isolated", action="store_true",
+                    help="skip the isolated-call timing under the reference's protocol")
     ap.add_argument("--workload",
                     choices=["gemv", "llama7b", "llama70b", "llama7b-tp", "llama70b-tp"],
                     default="gemv",
