@@ -265,23 +265,30 @@ __global__ void __launch_bounds__(vb::kThreads, 1)
       if (!mbar_wait_spin_bounded(&full[slot], (s / nst) & 1, abort_flag)) break;
       if (s >= nbb && !mbar_wait_spin_bounded(&bfree[b], ((s / nbb) - 1) & 1, abort_flag)) break;
       const uint32_t raw = rawbase + slot * raw_stage, dst = bbase + b * b_buf;
-      for (int q = t; q < words; q += kDqWarps * 32) {
-        const int n = q >> 4, w = q & 15;  // tile row n, word w (k = 8w .. 8w + 7)
-        uint32_t word;
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(word) : "r"(raw + n * kRawRowBytes + w * 4));
+      // Four words of one row per trip (one 16-byte load, one scale, four
+      // independent unpack chains): quad u = 4n + v holds words 4v .. 4v + 3
+      // of tile row n, all in swizzle atom v / 2.
+      for (int u = t; u < words / 4; u += kDqWarps * 32) {
+        const int n = u >> 2, w0 = (u & 3) << 2;  // tile row n, words w0 .. w0 + 3
+        const uint4 wq = lds128(raw + n * kRawRowBytes + w0 * 4);
+        const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
         const __half sc = scs[n * groups + s];
         const __half2 s2 = __halves2half2(sc, sc);
-        uint32_t h[4];
-        unpack_q8(word, h);  // (q0,q4), (q1,q5), (q2,q6), (q3,q7)
-        uint32_t o[4] = {prmt(h[0], h[1], 0x5410u), prmt(h[2], h[3], 0x5410u),
-                         prmt(h[0], h[1], 0x7632u), prmt(h[2], h[3], 0x7632u)};
+        const uint32_t row = dst + (w0 >> 3) * b_atom + (n >> 3) * 1024 + (n & 7) * 128;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&o[i]), s2);
-          o[i] = *reinterpret_cast<const uint32_t*>(&v);
+        for (int e = 0; e < 4; ++e) {
+          uint32_t h[4];
+          unpack_q8(wv[e], h);  // (q0,q4), (q1,q5), (q2,q6), (q3,q7)
+          uint32_t o[4] = {prmt(h[0], h[1], 0x5410u), prmt(h[2], h[3], 0x5410u),
+                           prmt(h[0], h[1], 0x7632u), prmt(h[2], h[3], 0x7632u)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&o[i]), s2);
+            o[i] = *reinterpret_cast<const uint32_t*>(&v);
+          }
+          const int j = (w0 & 7) + e;  // 16-byte chunk of the 128-byte swizzled row
+          sts128(row + ((j ^ (n & 7)) << 4), o);
         }
-        const int a = w >> 3, j = w & 7;
-        sts128(dst + a * b_atom + (n >> 3) * 1024 + (n & 7) * 128 + ((j ^ (n & 7)) << 4), o);
       }
       fence_async_shared();
       __syncwarp();
