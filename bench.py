@@ -240,7 +240,8 @@ def time_reference_cuda(M, K, B, sets=64, chain_steps=20):
     reference, compiled unmodified for sm_100a (oracle/_ref, built from the
     checkout by oracle/Makefile), called through its host entry point
     w4a16_gemv (gemv_w4a16.cu:568-591: stamp reset copy + launch).  Its best
-    kernel (v1) and its default (v5), each (a) isolated under the reference's
+    kernel (v1), its default (v5) and, for B > 1, its weight-reuse batch path,
+    each (a) isolated under the reference's
     protocol and (b) over the same 64-matrix chain as this library's
     ``value``, launched back to back.  None when there is no GPU or the
     reference was not built."""
@@ -263,16 +264,20 @@ def time_reference_cuda(M, K, B, sets=64, chain_steps=20):
     out = {"build": "reference csrc/gemv_w4a16.cu, unmodified, nvcc -O3 --use_fast_math "
                     "for sm_100a (its setup.py flags)",
            "per_gemv_bytes": gemv_bytes(M, K, B)}
-    for name, ver in (("v1", 1), ("v5", 5)):
-        iso = time_isolated(torch, lambda: ref_cuda.gemv(packed[0], scales[0], x, y, version=ver))
+    kernels = [("v1", 1, False), ("v5", 5, False)]
+    if B > 1:
+        kernels.append(("reuse", 5, True))  # its batch path (gemv_w4a16.cu:364-413)
+    for name, ver, reuse in kernels:
+        iso = time_isolated(torch, lambda: ref_cuda.gemv(packed[0], scales[0], x, y, version=ver,
+                                                         reuse_weights=reuse))
         for _ in range(3):
             for s in range(sets):
-                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver)
+                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver, reuse_weights=reuse)
         torch.cuda.synchronize()
         e0.record()
         for _ in range(chain_steps):
             for s in range(sets):
-                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver)
+                ref_cuda.gemv(packed[s], scales[s], x, y, version=ver, reuse_weights=reuse)
         e1.record()
         torch.cuda.synchronize()
         chain = e0.elapsed_time(e1) * 1e3 / (chain_steps * sets)
