@@ -2,7 +2,7 @@
 
 The partitioning arithmetic -- which rows / which whole 128-wide groups of K
 each rank owns -- and the exchange it implies are checked with gloo process
-groups (world 2 and 3, spawned ranks on 127.0.0.1): every rank computes its
+groups (world 2, 3 and 4, spawned ranks on 127.0.0.1): every rank computes its
 shard with the CPU oracle, the ranks all-gather (row-parallel) or all-reduce
 (K-parallel) through torch.distributed, and the result must equal the oracle
 on the whole matrix.  The CUDA kernels are exercised by test_sharded_gpu.py.
@@ -103,13 +103,13 @@ def _rank_main(rank: int, world: int, port: int, layout: str, M: int, K: int, B:
 
 
 @pytest.mark.parametrize("layout", ["row", "k"])
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_gloo_exchange_matches_whole_matrix(layout, world, tmp_path):
     import torch.multiprocessing as mp
 
     from oracle import oracle as O
 
-    M, K, B = 96, 1408, 2  # 11 groups: K slices of unequal size at world 2 and 3
+    M, K, B = 96, 1408, 2  # 11 groups: K slices of unequal size at world 2, 3 and 4
     out = str(tmp_path / "y")
     mp.start_processes(_rank_main, args=(world, _free_port(), layout, M, K, B, out),
                        nprocs=world, start_method="spawn", join=True)
@@ -216,12 +216,12 @@ def _tp_rank_main(rank: int, world: int, port: int, out_path: str) -> None:
 
 
 def _tp_problem():
-    I, K, M, B = 640, 256, 64, 2  # 5 blocks of 128: unequal splits at 2 and 3 ranks
+    I, K, M, B = 640, 256, 64, 2  # 5 blocks of 128: unequal splits at 2, 3 and 4 ranks
     return (make_problem(I, K, B, seed=95), make_problem(I, K, 1, seed=96),
             make_problem(M, I, 1, seed=97))
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_gloo_tensor_parallel_mlp_matches_whole_layer(world, tmp_path):
     # The row split of gate/up is the K split of down, so the ranks' partials
     # of down over their own h slices add up to the whole layer.
