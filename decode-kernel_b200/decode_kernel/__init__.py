@@ -114,6 +114,8 @@ def gemv_multi(weights, x: torch.Tensor, pdl: bool = False, reuse_weights: bool 
     for p, s in weights:
         if p.dtype != torch.int32 or s.dtype != torch.float16 or not (p.is_cuda and s.is_cuda):
             raise RuntimeError("packed must be CUDA int32 and scales CUDA fp16")
+        if p.device != x.device or s.device != x.device:
+            raise RuntimeError("packed and scales must be on x's device")
         if p.shape[1] * 8 != K or s.shape != (p.shape[0], K // GROUP_SIZE):
             raise RuntimeError("every matrix must be [M, K/8] with scales [M, K/128] for x's K")
         if not (p.is_contiguous() and s.is_contiguous()):
@@ -122,19 +124,22 @@ def gemv_multi(weights, x: torch.Tensor, pdl: bool = False, reuse_weights: bool 
           for p, _ in weights]
     flags = capi.DK_FLAG_PDL if pdl else 0
     cfg = capi.default_config(reuse_weights=int(bool(reuse_weights)), flags=flags)
-    capi.check(capi.gemv_multi([p.data_ptr() for p, _ in weights],
-                               [s.data_ptr() for _, s in weights],
-                               [p.shape[0] for p, _ in weights], [y.data_ptr() for y in ys],
-                               x.data_ptr(), K, x.shape[0], cfg,
-                               torch.cuda.current_stream(x.device).cuda_stream),
-               "dk_w4a16_gemv_multi")
+    with torch.cuda.device(x.device):  # the C ABI launches on the current device
+        capi.check(capi.gemv_multi([p.data_ptr() for p, _ in weights],
+                                   [s.data_ptr() for _, s in weights],
+                                   [p.shape[0] for p, _ in weights], [y.data_ptr() for y in ys],
+                                   x.data_ptr(), K, x.shape[0], cfg,
+                                   torch.cuda.current_stream(x.device).cuda_stream),
+                   "dk_w4a16_gemv_multi")
     return ys
 
 
-def _check_pair(packed: torch.Tensor, scales: torch.Tensor, K: int) -> None:
+def _check_pair(packed: torch.Tensor, scales: torch.Tensor, K: int, device: torch.device) -> None:
     if packed.dtype != torch.int32 or scales.dtype != torch.float16 or not (
             packed.is_cuda and scales.is_cuda):
         raise RuntimeError("packed must be CUDA int32 and scales CUDA fp16")
+    if packed.device != device or scales.device != device:
+        raise RuntimeError("packed and scales must be on x's device")
     if packed.dim() != 2 or packed.shape[1] * 8 != K or scales.shape != (packed.shape[0],
                                                                           K // GROUP_SIZE):
         raise RuntimeError("every matrix must be [M, K/8] with scales [M, K/128] for x's K")
@@ -156,18 +161,20 @@ def gemv_silu_mul(gate, up, x: torch.Tensor, pdl: bool = False, reuse_weights: b
     if x.dtype != torch.float16 or not x.is_cuda or not x.is_contiguous() or x.dim() != 2:
         raise RuntimeError("x must be a contiguous 2-D CUDA fp16 tensor")
     K = x.shape[1]
-    _check_pair(*gate, K)
-    _check_pair(*up, K)
+    _check_pair(*gate, K, x.device)
+    _check_pair(*up, K, x.device)
     if gate[0].shape != up[0].shape:
         raise RuntimeError("gate and up must have the same shape")
     M = gate[0].shape[0]
     h = torch.empty((x.shape[0], M), dtype=torch.float16, device=x.device)
     flags = capi.DK_FLAG_PDL if pdl else 0
     cfg = capi.default_config(reuse_weights=int(bool(reuse_weights)), flags=flags)
-    capi.check(capi.gemv_silu_mul(gate[0].data_ptr(), gate[1].data_ptr(), up[0].data_ptr(),
-                                  up[1].data_ptr(), x.data_ptr(), h.data_ptr(), M, K, x.shape[0],
-                                  cfg, torch.cuda.current_stream(x.device).cuda_stream),
-               "dk_w4a16_gemv_silu_mul")
+    with torch.cuda.device(x.device):  # the C ABI launches on the current device
+        capi.check(capi.gemv_silu_mul(gate[0].data_ptr(), gate[1].data_ptr(), up[0].data_ptr(),
+                                      up[1].data_ptr(), x.data_ptr(), h.data_ptr(), M, K,
+                                      x.shape[0], cfg,
+                                      torch.cuda.current_stream(x.device).cuda_stream),
+                   "dk_w4a16_gemv_silu_mul")
     return h
 
 

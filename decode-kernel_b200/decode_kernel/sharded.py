@@ -232,6 +232,22 @@ class PeerBuffers:
             pass
 
 
+def _as_batch(x: torch.Tensor, K: int, max_batch: int, dev: torch.device) -> torch.Tensor:
+    """x as [B, K] after the checks every layer makes before a launch: a
+    contiguous fp16 [B, K] tensor on the layer's GPU with B <= max_batch.
+    A tensor on another device would hand the kernels a pointer they cannot
+    read, so it is refused here."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if x.dim() != 2 or x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != K:
+        raise RuntimeError(f"x must be contiguous fp16 [B, {K}]")
+    if x.device != dev:
+        raise RuntimeError(f"x is on {x.device}, the layer's weights on {dev}")
+    if x.shape[0] > max_batch:
+        raise RuntimeError(f"batch {x.shape[0]} > max_batch {max_batch}")
+    return x
+
+
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
@@ -262,7 +278,7 @@ class RowParallelW4A16:
         self.max_batch = int(max_batch)
         if 2 * self.max_batch * self.M > peers.nbytes:
             raise ValueError("peer buffers too small for [max_batch, M] fp16")
-        dev = torch.device("cuda", torch.cuda.current_device())
+        dev = self.dev = torch.device("cuda", torch.cuda.current_device())
         self.shards = {}
         for r in peers.local_ranks():
             p, s, row0 = slice_rows(packed, scales, peers.world, r)
@@ -270,13 +286,8 @@ class RowParallelW4A16:
             self.shards[r] = (p.to(dev).clone(), s.to(dev).clone(), row0)
 
     def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
-        if x.dim() == 1:
-            x = x.unsqueeze(0)
+        x = _as_batch(x, self.K, self.max_batch, self.dev)
         B = x.shape[0]
-        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
-            raise RuntimeError("x must be contiguous fp16 [B, K]")
-        if B > self.max_batch:
-            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         if self.exchange == "nccl":
             return self._nccl(x)
         lib, st = self.peers.lib, _stream()
@@ -339,7 +350,7 @@ class KParallelW4A16:
         self.max_batch = int(max_batch)
         if 8 * peers.world * self.max_batch * self.M > peers.nbytes:
             raise ValueError("peer buffers too small for [world, max_batch, M] 64-bit words")
-        dev = torch.device("cuda", torch.cuda.current_device())
+        dev = self.dev = torch.device("cuda", torch.cuda.current_device())
         self.shards = {}
         for r in peers.local_ranks():
             p, s, k0 = slice_k(packed, scales, peers.world, r)
@@ -348,13 +359,8 @@ class KParallelW4A16:
                     for r in self.shards}
 
     def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
-        if x.dim() == 1:
-            x = x.unsqueeze(0)
+        x = _as_batch(x, self.K, self.max_batch, self.dev)
         B = x.shape[0]
-        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
-            raise RuntimeError("x must be contiguous fp16 [B, K]")
-        if B > self.max_batch:
-            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         if self.exchange == "nccl":
             return self._nccl(x)
         lib, st = self.peers.lib, _stream()
@@ -391,6 +397,8 @@ class KParallelW4A16:
             kn = self.shards[r][0].shape[1] * 8
             if x.dtype != torch.float16 or not x.is_contiguous() or x.dim() != 2 or x.shape[1] != kn:
                 raise RuntimeError(f"rank {r}: x must be contiguous fp16 [B, {kn}]")
+            if x.device != self.dev:
+                raise RuntimeError(f"rank {r}: x is on {x.device}, the layer's weights on {self.dev}")
             if B is not None and x.shape[0] != B:
                 raise RuntimeError("every rank's x must have the same batch")
             B = x.shape[0]
@@ -495,7 +503,7 @@ class TensorParallelMLP:
         self.M, self.peers, self.max_batch = pd.shape[0], peers, int(max_batch)
         if self.I // GROUP_SIZE < peers.world:
             raise ValueError("fewer 128-wide blocks of the intermediate size than ranks")
-        dev = torch.device("cuda", torch.cuda.current_device())
+        dev = self.dev = torch.device("cuda", torch.cuda.current_device())
         self.gu, self.h = {}, {}
         for r in peers.local_ranks():
             i0, n = split_dim(self.I, peers.world, r)
@@ -505,13 +513,8 @@ class TensorParallelMLP:
                                    group=group)
 
     def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
-        if x.dim() == 1:
-            x = x.unsqueeze(0)
+        x = _as_batch(x, self.K, self.max_batch, self.dev)
         B = x.shape[0]
-        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
-            raise RuntimeError("x must be contiguous fp16 [B, K]")
-        if B > self.max_batch:
-            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         cfg, st = _cfg(pdl), _stream()
         for r, (pg, sg, pu, su) in self.gu.items():
             _check(capi.gemv_silu_mul(pg.data_ptr(), sg.data_ptr(), pu.data_ptr(), su.data_ptr(),
@@ -546,7 +549,7 @@ class TensorParallelAttentionProj:
         self.M, self.peers, self.max_batch = po.shape[0], peers, int(max_batch)
         if min(self.Q, self.KV) // GROUP_SIZE < peers.world:
             raise ValueError("fewer 128-wide heads than ranks")
-        dev = torch.device("cuda", torch.cuda.current_device())
+        dev = self.dev = torch.device("cuda", torch.cuda.current_device())
         self.qkv, self.outs = {}, {}
         for r in peers.local_ranks():
             q0, nq = split_dim(self.Q, peers.world, r)
@@ -559,13 +562,8 @@ class TensorParallelAttentionProj:
                                 group=group)
 
     def __call__(self, x: torch.Tensor, attn=None, pdl: bool = False) -> torch.Tensor:
-        if x.dim() == 1:
-            x = x.unsqueeze(0)
+        x = _as_batch(x, self.K, self.max_batch, self.dev)
         B = x.shape[0]
-        if x.dtype != torch.float16 or not x.is_contiguous() or x.shape[1] != self.K:
-            raise RuntimeError("x must be contiguous fp16 [B, K]")
-        if B > self.max_batch:
-            raise RuntimeError(f"batch {B} > max_batch {self.max_batch}")
         cfg, st = _cfg(pdl), _stream()
         att = {}
         for r, mats in self.qkv.items():

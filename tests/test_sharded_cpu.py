@@ -251,3 +251,23 @@ def test_split_dim_is_head_aligned():
         assert parts == [k_range(n, world, r) for r in range(world)]
         assert all(k0 % 128 == 0 and kn % 128 == 0 and kn > 0 for k0, kn in parts)
         assert sum(kn for _, kn in parts) == n
+
+
+def test_layer_inputs_are_checked_before_any_launch():
+    # Every sharded layer passes x through this check before it hands a
+    # pointer to the kernels; a tensor on another device is refused.
+    import torch
+
+    from decode_kernel.sharded import _as_batch
+
+    cpu, gpu = torch.device("cpu"), torch.device("cuda", 0)
+    x = torch.zeros(2, 256, dtype=torch.float16)
+    assert _as_batch(x, 256, 2, cpu) is x
+    assert _as_batch(x[0], 256, 1, cpu).shape == (1, 256)
+    with pytest.raises(RuntimeError, match="is on cpu"):
+        _as_batch(x, 256, 2, gpu)
+    with pytest.raises(RuntimeError, match="max_batch"):
+        _as_batch(x, 256, 1, cpu)
+    for bad in (x.float(), x[:, :128], x.t(), x.reshape(2, 2, 128)):
+        with pytest.raises(RuntimeError, match="contiguous fp16"):
+            _as_batch(bad, 256, 2, cpu)
