@@ -271,3 +271,79 @@ def test_layer_inputs_are_checked_before_any_launch():
     for bad in (x.float(), x[:, :128], x.t(), x.reshape(2, 2, 128)):
         with pytest.raises(RuntimeError, match="contiguous fp16"):
             _as_batch(bad, 256, 2, cpu)
+
+
+# --- failure detection on the host: a rank that leaves or never joins ------
+#
+# Ranks are gloo processes on the CPU and the failures are made on the host;
+# nothing here touches a GPU.  The process group is created as the sharded
+# benches create theirs, with a short timeout, so the surviving ranks end
+# their next collective (or the rendezvous) with an error instead of waiting.
+
+_FAIL_TIMEOUT_S = 5
+
+
+def _fail_rank_main(rank: int, world: int, port: int, mode: str, out_path: str) -> None:
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    t0 = time.monotonic()
+
+    def record(what: str) -> None:
+        with open(f"{out_path}.{rank}", "w") as f:
+            f.write(f"{what} {time.monotonic() - t0:.1f}")
+
+    if mode == "never_joins" and rank == world - 1:
+        return
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world,
+                                timeout=datetime.timedelta(seconds=_FAIL_TIMEOUT_S))
+    except Exception:  # the rendezvous gave up on the missing rank
+        record("init_error")
+        return
+    x = torch.ones(64)
+    try:
+        dist.all_reduce(x)  # step 1: every rank takes part
+        if mode == "exits" and rank == world - 1:
+            record("left")
+            return  # this rank leaves between steps, with no collective in flight
+        dist.all_reduce(x)  # step 2: the survivors must get an error, not hang
+        record("no_error")
+    except Exception:
+        record("step_error")
+
+
+@pytest.mark.parametrize("mode", ["exits", "never_joins"])
+def test_lost_rank_ends_the_survivors_collective_with_an_error(mode, tmp_path):
+    import time
+
+    import torch.multiprocessing as mp
+
+    world = 3
+    out = str(tmp_path / "r")
+    ctx = mp.start_processes(_fail_rank_main, args=(world, _free_port(), mode, out),
+                             nprocs=world, start_method="spawn", join=False)
+    deadline = time.monotonic() + 120
+    while not ctx.join(timeout=5):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("ranks still running after 120 s")
+    results = {}
+    for r in range(world):
+        path = f"{out}.{r}"
+        if os.path.exists(path):
+            what, secs = open(path).read().split()
+            results[r] = (what, float(secs))
+    want = "step_error" if mode == "exits" else "init_error"
+    for r in range(world - 1):
+        assert results[r][0] == want, results
+        assert results[r][1] < 4 * _FAIL_TIMEOUT_S + 10, results
+    if mode == "exits":
+        assert results[world - 1][0] == "left"
+    else:
+        assert world - 1 not in results
