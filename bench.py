@@ -95,6 +95,39 @@ def ncu_traffic_per_launch(m: int, k: int, b: int):
     return None
 
 
+def run_meta(gpu_index=None) -> dict:
+    """Provenance of a result line, as the reference's bench JSON records it
+    (bench/common.py:18-52): GPU, driver, torch and CUDA versions, source
+    revision, host threads, UTC time.  Best effort: a field whose source is
+    missing (no GPU, no nvidia-smi, no git checkout) is None, and nothing
+    here raises."""
+    meta = {"timestamp": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
+            "host_threads": os.cpu_count(), "torch": None, "cuda": None, "gpu": None,
+            "driver": None, "git": None}
+    try:
+        import torch
+
+        meta["torch"], meta["cuda"] = torch.__version__, torch.version.cuda
+        if gpu_index is not None and torch.cuda.is_available():
+            prop = torch.cuda.get_device_properties(gpu_index)
+            meta["gpu"] = {"name": prop.name, "sm_count": prop.multi_processor_count,
+                           "cc": f"{prop.major}.{prop.minor}",
+                           "memory_gib": round(prop.total_memory / 2**30, 1)}
+    except Exception:
+        pass
+    for key, cmd in (("driver", ["nvidia-smi", "--query-gpu=driver_version",
+                                 "--format=csv,noheader"]),
+                     ("git", ["git", "rev-parse", "--short", "HEAD"])):
+        try:
+            out = subprocess.run(cmd, cwd=REPO, capture_output=True, text=True, timeout=10)
+            text = out.stdout.strip()
+            if out.returncode == 0 and text:
+                meta[key] = text.splitlines()[0].strip()
+        except Exception:
+            pass
+    return meta
+
+
 class ClockSampler:
     """nvidia-smi samples during the timed region (recipe's clocks line)."""
 
@@ -340,6 +373,7 @@ def run_reference(args) -> None:
         rc = time_reference_cuda(M, K, B)
         if rc is not None:
             line["reference_cuda_same_gpu"] = rc
+    line["meta"] = run_meta(None)
     print(json.dumps(line), flush=True)
 
 
@@ -592,6 +626,7 @@ def run_ours(args) -> None:
         line["isolated"] = isolated
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    line["meta"] = run_meta(local)
     print(json.dumps(line), flush=True)
 
 
@@ -713,6 +748,7 @@ def run_sharded(args) -> None:
                    "l2": "inputs larger than L2 (the step streams every layer's weights)"},
         "device_error": err, "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
     }
+    line["meta"] = run_meta(local)
     print(json.dumps(line), flush=True)
 
 
@@ -837,6 +873,7 @@ def run_tensor_parallel(args) -> None:
                    "l2": "inputs larger than L2 (the step streams every layer's weights)"},
         "device_error": err, "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
     }
+    line["meta"] = run_meta(local)
     print(json.dumps(line), flush=True)
 
 

@@ -3,7 +3,9 @@
 The reference arm (``--impl reference``) times the CPU restatement of the
 reference's fp32 dequantize-then-matmul on the host cores, so it runs here:
 its JSON line must carry the keys the driver reads.  Ranks other than 0 print
-nothing and exit 0.  The headline metric name must be BASELINE.json's.
+nothing and exit 0.  The headline metric name must be BASELINE.json's, and
+every line carries its provenance (``meta``) without failing when a source of
+it is missing.
 """
 
 from __future__ import annotations
@@ -51,6 +53,8 @@ def test_reference_arm_line_on_host_cores():
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+    meta = d["meta"]
+    assert meta["torch"] and meta["host_threads"] >= 1 and meta["timestamp"].endswith("Z")
 
 
 def test_reference_arm_other_ranks_exit_quietly():
@@ -58,3 +62,13 @@ def test_reference_arm_other_ranks_exit_quietly():
                "--no-reference-cuda", env={"WORLD_SIZE": "2", "RANK": "1", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_run_meta_never_raises_without_a_gpu():
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    for gpu in (None, 0):
+        meta = bench.run_meta(gpu)
+        json.dumps(meta)
+        assert set(meta) >= {"timestamp", "host_threads", "torch", "cuda", "gpu", "driver", "git"}
