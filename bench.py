@@ -378,6 +378,149 @@ def run_reference(args) -> None:
 
 
 # --------------------------------------------------------------------------
+# Same-precision peer: Marlin (as vLLM ships it) on the same GPU
+# --------------------------------------------------------------------------
+
+def run_marlin_peer(args) -> None:
+    """Marlin's W4A16 GEMM, the same-precision peer the reference never ran,
+    on this GPU and on the workload of ``value``.
+
+    This library's weights become GPTQ tensors (``decode_kernel.gptq.to_gptq``,
+    exact), then go through vLLM's own loading steps for a symmetric uint4b8
+    checkpoint without act-order (vllm/model_executor/kernels/linear/
+    mixed_precision/marlin.py: ``gptq_marlin_repack``, ``marlin_permute_scales``,
+    empty g_idx and zero points, ``marlin_make_workspace_new``), and run with
+    vLLM's ``apply_gptq_marlin_linear``.  One full output is checked against
+    the CPU oracle (max abs < 1e-2) before anything is timed.  Timed like
+    ``value`` (S distinct matrices per step, a CUDA graph of one step when it
+    captures, else eager launches) and like ``isolated``.  Rank 0 only.
+    Prints one JSON line with "impl": "marlin (vLLM ...)", or an
+    "unavailable" line when there is no GPU or vLLM lacks its Marlin ops."""
+    ws, rank, local = dist_info()
+    if rank != 0:
+        return
+    import torch
+
+    name = "marlin (vLLM)"
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": name, "unavailable": "no CUDA device"}), flush=True)
+        return
+    try:
+        import vllm
+        from vllm import _custom_ops as ops
+        from vllm.model_executor.layers.quantization.utils.marlin_utils import (
+            apply_gptq_marlin_linear, marlin_make_empty_g_idx, marlin_make_workspace_new,
+            marlin_permute_scales)
+        from vllm.scalar_type import scalar_types
+
+        if not hasattr(torch.ops._C, "marlin_gemm"):
+            raise ImportError("this vLLM build has no marlin_gemm")
+        name = f"marlin (vLLM {vllm.__version__})"
+    except Exception as e:  # noqa: BLE001 -- any import failure means no peer
+        print(json.dumps({"impl": name, "unavailable": f"{type(e).__name__}: {e}"[:300]}),
+              flush=True)
+        return
+    import numpy as np
+
+    from decode_kernel.gptq import to_gptq
+    from decode_kernel.quantize import quantize_and_pack_cuda
+    from oracle import oracle as O
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    M, K, B, S = args.m, args.k, args.batch, args.sets
+    per_gemv = gemv_bytes(M, K, B)
+    empty = marlin_make_empty_g_idx(dev)
+    workspace = marlin_make_workspace_new(dev)
+    mats, xs, first = [], [], None
+    for s in range(S):
+        g = torch.Generator(device=dev).manual_seed(s)
+        w = torch.randn(M, K, generator=g, device=dev) * 0.02
+        p, sc = quantize_and_pack_cuda(w)
+        del w
+        if first is None:
+            first = (p.cpu().numpy(), sc.cpu().view(torch.int16).numpy().view(np.uint16))
+        t = to_gptq(p, sc)
+        try:
+            wq = ops.gptq_marlin_repack(t.qweight, perm=empty, size_k=K, size_n=M, num_bits=4)
+        except RuntimeError as e:  # e.g. no kernel image for this GPU
+            print(json.dumps({"impl": name, "unavailable": f"gptq_marlin_repack: {e}"[:300]}),
+                  flush=True)
+            return
+        wsc = marlin_permute_scales(t.scales, size_k=K, size_n=M, group_size=128)
+        mats.append((wq, wsc))
+        xs.append(torch.randn(B, K, generator=g, device=dev).half())
+        del p, sc, t
+    torch.cuda.synchronize()
+
+    def call(s):
+        return apply_gptq_marlin_linear(
+            input=xs[s], weight=mats[s][0], weight_scale=mats[s][1], weight_zp=empty,
+            g_idx=empty, g_idx_sort_indices=empty, workspace=workspace,
+            wtype=scalar_types.uint4b8, output_size_per_partition=M,
+            input_size_per_partition=K, is_k_full=True)
+
+    # Parity before timing: the whole first output against the CPU oracle.
+    try:
+        y0 = call(0)
+        torch.cuda.synchronize()
+    except RuntimeError as e:  # e.g. no Marlin kernel image for this GPU
+        print(json.dumps({"impl": name, "unavailable": f"marlin_gemm: {e}"[:300]}), flush=True)
+        return
+    ref = O.linear_fp32(xs[0].cpu().view(torch.int16).numpy().view(np.uint16), *first)
+    err = float(np.abs(y0.float().cpu().numpy() - ref).max())
+    line = {"impl": name, "metric": metric_name(M, K, B), "unit": "GB/s", "n_gpus": 1,
+            "higher_is_better": True, "dtype": "int4*f16 (uint4b8, group 128)",
+            "data": "synthetic", "parity_max_abs_err": err,
+            "config": {"workload": f"{M}x{K} W4A16 GEMV B={B}", "M": M, "K": K,
+                       "global_batch": B, "gemvs_per_step": S}}
+    if not err < 1e-2:
+        line.update(value=None, error="Marlin output differs from the oracle by more than 1e-2")
+        print(json.dumps(line), flush=True)
+        return
+
+    def step():
+        for s in range(S):
+            call(s)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    graph, launch = None, "CUDA graph of one step, replayed"
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001 -- capture refused: time eager launches
+        graph, launch = None, f"eager launches (graph capture failed: {type(e).__name__})"
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    us = ms * 1e3 / (args.steps * S)
+    iso = time_isolated(torch, lambda: call(0))
+    del graph
+    line.update(value=per_gemv / (us * 1e-6) / 1e9, steps=args.steps, warmup=args.warmup,
+                ms_per_step=ms / args.steps, us_per_gemv=us, clocks=clocks.summary(),
+                isolated={"us_per_gemv": iso, "GBps": per_gemv / (iso * 1e-6) / 1e9,
+                          "protocol": "512 MiB fill flush, CUDA events around one call, "
+                                      "median of 200 after 20 warm-up"})
+    line["config"]["launch"] = launch
+    line["meta"] = run_meta(local)
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
 # GPU path
 # --------------------------------------------------------------------------
 
@@ -882,7 +1025,8 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "marlin"], default="ours",
+                    help="marlin: the same-precision peer (vLLM's Marlin) on this GPU")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=1)
@@ -909,6 +1053,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "marlin":
+        run_marlin_peer(args)
     elif args.workload.endswith("-tp"):
         run_tensor_parallel(args)
     elif args.workload != "gemv":

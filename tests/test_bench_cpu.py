@@ -72,3 +72,55 @@ def test_run_meta_never_raises_without_a_gpu():
         meta = bench.run_meta(gpu)
         json.dumps(meta)
         assert set(meta) >= {"timestamp", "host_threads", "torch", "cuda", "gpu", "driver", "git"}
+
+
+def test_marlin_peer_without_a_gpu_prints_unavailable():
+    r = _bench("--impl", "marlin", "--steps", "1", "--warmup", "3")
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(ln) for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert lines == [{"impl": "marlin (vLLM)", "unavailable": "no CUDA device"}]
+
+
+_MARLIN_HOST_CHECK = """
+import sys
+import torch
+try:
+    from vllm.model_executor.layers.quantization.utils.marlin_utils import (
+        apply_gptq_marlin_linear, marlin_make_empty_g_idx, marlin_make_workspace_new,
+        marlin_permute_scales)
+    from vllm.scalar_type import scalar_types
+except Exception as e:
+    print("SKIP", type(e).__name__, e)
+    sys.exit(0)
+from decode_kernel.gptq import to_gptq
+from decode_kernel.quantize import quantize_and_pack
+
+M, K = 256, 512
+packed, scales = quantize_and_pack(torch.randn(M, K) * 0.02)
+g = to_gptq(packed, scales)
+s = marlin_permute_scales(g.scales, size_k=K, size_n=M, group_size=128)
+assert tuple(s.shape) == (K // 128, M) and s.dtype == torch.float16
+assert torch.equal(s.flatten().sort().values, g.scales.flatten().sort().values)
+assert scalar_types.uint4b8.size_bits == 4
+print("OK")
+"""
+
+
+def test_marlin_peer_host_steps_accept_the_gptq_tensors():
+    # The host-side half of the peer's weight loading, on the CPU and in a
+    # child process (importing vLLM changes process-wide state): the names
+    # bench.py imports from vLLM exist, and vLLM's scale permutation takes the
+    # scales that to_gptq produces (a permutation of the same values).  The
+    # repack and the GEMM are GPU ops.
+    import pytest
+
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([str(REPO / "decode-kernel_b200"), str(REPO),
+                                         env.get("PYTHONPATH", "")])
+    r = subprocess.run([sys.executable, "-c", _MARLIN_HOST_CHECK], cwd=REPO, env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = r.stdout.strip().splitlines()[-1]
+    if out.startswith("SKIP"):
+        pytest.skip(out)
+    assert out == "OK"
