@@ -15,12 +15,14 @@ the library.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
 _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "_ref" / "libdkref.so"
-REF_CHECKOUT = Path("/root/reference")
+# The reference checkout; DK_REFERENCE overrides it, as for tests/golden/make_golden.py.
+REF_CHECKOUT = Path(os.environ.get("DK_REFERENCE", "/root/reference"))
 _lib = None
 
 
