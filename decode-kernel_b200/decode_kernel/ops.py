@@ -99,6 +99,18 @@ class W4A16Linear(torch.nn.Module):
         packed, scales = quantize_and_pack_cuda(w)
         return cls(packed, scales)
 
+    @classmethod
+    def from_gptq(cls, qweight: torch.Tensor, scales: torch.Tensor,
+                  qzeros: Optional[torch.Tensor] = None, g_idx: Optional[torch.Tensor] = None, *,
+                  zeros_minus_one: bool = False) -> "W4A16Linear":
+        """A layer from a symmetric 4-bit GPTQ checkpoint's tensors (group 128,
+        no act-order), converted exactly by ``decode_kernel.gptq.from_gptq``;
+        the buffers stay on the tensors' device."""
+        from .gptq import from_gptq
+
+        packed, s = from_gptq(qweight, scales, qzeros, g_idx, zeros_minus_one=zeros_minus_one)
+        return cls(packed, s)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return torch.ops.decode_kernel.w4a16_linear(x, self.packed, self.scales)
 

@@ -132,3 +132,16 @@ def test_rejects_what_the_format_cannot_hold():
         to_gptq(torch.from_numpy(pack_library(q)).to(torch.int64), s)
     with pytest.raises(ValueError, match="scales"):
         to_gptq(torch.from_numpy(pack_library(q)), s[:, :-1])
+
+
+def test_linear_module_from_gptq_checkpoint():
+    from decode_kernel import W4A16Linear
+
+    q, s, qweight, qzeros = golden("m40_k1024")
+    g_idx = torch.arange(q.shape[1], dtype=torch.int32) // 128
+    layer = W4A16Linear.from_gptq(qweight, s.t().contiguous(), qzeros, g_idx)
+    assert (layer.out_features, layer.in_features) == q.shape
+    np.testing.assert_array_equal(layer.packed.numpy(), pack_library(q))
+    assert torch.equal(layer.scales, s)
+    with pytest.raises(ValueError, match="zero points"):
+        W4A16Linear.from_gptq(qweight, s.t().contiguous(), qzeros, zeros_minus_one=True)
