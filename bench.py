@@ -25,8 +25,21 @@ cpu_baseline / --impl reference
         python/decode_kernel/reference.py:17-26) restated in numpy
         (oracle/oracle.py: linear_fp32_np), timed on the host cores.
 
-Multi-GPU (torchrun, one rank per GPU): each rank streams its own weight
-stack (weak scaling, no data-path collective); time = max over ranks.
+baseline_configs (one GPU)
+        the other BASELINE configurations under the same two protocols
+        (chain and isolated): the Llama-7B MLP shapes 11008x4096 and
+        4096x11008, the 70B-shaped 28672x8192 and 8192x28672 at B = 1 and 8,
+        and the 4096^2 batch sweep B in {1, 2, 4, 8, 16, 32}; each with µs,
+        GB/s, the fraction of the measured roof and an oracle spot check.
+strong_scaling
+        the 70B-shaped decoder layers' projections (8 layers, B = 1) in the
+        tensor-parallel layout over every rank of the run -- the same command
+        at N = 1 -- with the fused NVLink exchange; rank 0 checks layer 0
+        against the unsharded layer before timing.
+
+Multi-GPU (torchrun, one rank per GPU): for ``value`` each rank streams its
+own weight stack (weak scaling, no data-path collective); time = max over
+ranks.  ``strong_scaling`` shards one model over the ranks.
 """
 
 from __future__ import annotations
@@ -56,6 +69,20 @@ def gemv_bytes(m: int, k: int, b: int) -> int:
     """Algorithmic bytes of one GEMV: packed W + scales + x + y
     (bench/common.py:111-117 of the reference)."""
     return m * (k // 2) + m * (k // 128) * 2 + b * k * 2 + b * m * 2
+
+
+def workload_config(m: int, k: int, b: int, sets: int, ws: int) -> dict:
+    """The workload, as both arms report it under ``config`` -- the same dict
+    from this library's arm and from the reference arm, so the two lines say
+    that they measured the same thing.  How each arm runs it goes under
+    ``arm``."""
+    per = gemv_bytes(m, k, b)
+    return {"workload": f"{m}x{k} W4A16 GEMV B={b}", "M": m, "K": k, "global_batch": b * ws,
+            "gemvs_per_step": sets,
+            "l2": f"inputs larger than L2: {sets} distinct weight sets "
+                  f"({sets * per / 2**20:.0f} MiB) cycled, no flush",
+            "parallelism": f"x{ws}: independent weight stacks per GPU (weak scaling), "
+                           f"no collective"}
 
 
 # --------------------------------------------------------------------------
@@ -360,8 +387,10 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": f"{M}x{K} W4A16 GEMV B={B}", "M": M, "K": K, "global_batch": B,
-                   "parallelism": "host cores (rank 0 only)"},
+        "config": workload_config(M, K, B, args.sets, ws),
+        "arm": {"runs_on": f"host cores of rank 0 ({cores} threads); other ranks exit",
+                "step": f"a bounded sample of the workload: rows [0, {rows}) of one {M}x{K} "
+                        f"matrix per step"},
         "cpu_baseline": {
             "value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"each step: rows [0, {rows}) of the {M}x{K} matrix, x [{B},{K}]; "
@@ -524,6 +553,296 @@ def run_marlin_peer(args) -> None:
 # GPU path
 # --------------------------------------------------------------------------
 
+def kernel_path(m: int, k: int, b: int) -> str:
+    """Which kernel dk_w4a16_gemv's default dispatch (version 5) runs for a
+    pass of ``b`` <= 32 rows (the host dispatch in dk_gemv.cu)."""
+    if b <= 8:
+        return "k_stream (v5, 1 n-tile)"
+    if b > 16 and m >= 16384 and k % 128 == 0:
+        return "k_batch (tcgen05)"
+    return f"k_stream (v5, {2 if b <= 16 else 4} n-tiles)"
+
+
+def make_stack(torch, quantize, dev, m: int, k: int, b: int, sets: int, seed0: int):
+    """``sets`` distinct seeded W ~ N(0, 0.02) [m, k], quantized on the GPU
+    (bit-exact with the CPU quantizer), each with its own x ~ N(0, 1) [b, k]
+    and output [b, m]."""
+    packed, scales, xs, ys = [], [], [], []
+    for s in range(sets):
+        g = torch.Generator(device=dev).manual_seed(seed0 + s)
+        w = torch.randn(m, k, generator=g, device=dev) * 0.02
+        p, sc = quantize(w)
+        del w
+        packed.append(p)
+        scales.append(sc)
+        xs.append(torch.randn(b, k, generator=g, device=dev).half())
+        ys.append(torch.empty(b, m, dtype=torch.float16, device=dev))
+    torch.cuda.synchronize()
+    return packed, scales, xs, ys
+
+
+def time_chain_us(torch, capi, packed, scales, xs, ys, m, k, b, cfg, steps: int) -> float:
+    """µs per GEMV over ``steps`` replays of a CUDA graph that runs one C-ABI
+    GEMV per weight set, back to back (PDL when ``cfg`` asks for it) -- the
+    protocol of ``value``."""
+    nsets = len(packed)
+
+    def step(stream):
+        for i in range(nsets):
+            st = capi.gemv(packed[i].data_ptr(), scales[i].data_ptr(), xs[i].data_ptr(),
+                           ys[i].data_ptr(), m, k, b, cfg, 0, 0, stream)
+            if st:
+                capi.check(st, "dk_w4a16_gemv")
+
+    for _ in range(3):
+        step(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / (steps * nsets)
+
+
+def spot_check(torch, packed, scales, x, y, rows: int = 64) -> float:
+    """Max abs error of the first ``rows`` outputs against the CPU oracle
+    (outside every timed region)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    pk = packed[:rows].cpu().numpy()
+    sc = scales[:rows].cpu().view(torch.int16).numpy().view(np.uint16)
+    xx = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    ref = O.linear_fp32(xx, pk, sc)
+    return float(np.abs(y[:, :rows].float().cpu().numpy() - ref).max())
+
+
+# The other BASELINE configurations, each timed under the headline's two
+# protocols: the Llama-7B MLP shapes (config 2), the 70B-shaped layers on one
+# GPU at B = 1 and 8 (config 5's per-GPU shapes) and the 4096^2 batch sweep
+# (config 3).
+SWEEP_SHAPES = [(11008, 4096, 1), (4096, 11008, 1), (28672, 8192, 1), (8192, 28672, 1),
+                (28672, 8192, 8), (8192, 28672, 8)]
+SWEEP_BATCHES = [1, 2, 4, 8, 16, 32]
+
+
+def run_sweeps(args, torch, capi, quantize, dev, packed, scales, peak: float) -> dict:
+    """Per-shape and per-batch lines for the BASELINE configs besides the
+    headline: µs per GEMV in the chain (``value``'s protocol) and isolated
+    (the reference's), GB/s and the fraction of the measured roof; each
+    checked against the CPU oracle on its first 64 rows before timing."""
+    cfg = capi.default_config(flags=0 if args.no_pdl else capi.DK_FLAG_PDL)
+    plain = capi.default_config()
+    steps = max(args.steps, 20)
+
+    def entry(m, k, b, pk, sc, xs, ys):
+        err = spot_check(torch, pk[0], sc[0], xs[0], ys[0])
+        assert err < 1e-2, f"sweep spot check {m}x{k} B={b}: {err}"
+        us = time_chain_us(torch, capi, pk, sc, xs, ys, m, k, b, cfg, steps)
+        st = torch.cuda.current_stream().cuda_stream
+        iso = time_isolated(torch, lambda: capi.check(
+            capi.gemv(pk[0].data_ptr(), sc[0].data_ptr(), xs[0].data_ptr(), ys[0].data_ptr(),
+                      m, k, b, plain, 0, 0, st), "dk_w4a16_gemv"), iters=100, warmup=10)
+        nbytes = gemv_bytes(m, k, b)
+        return {"M": m, "K": k, "B": b, "kernel": kernel_path(m, k, b), "sets": len(pk),
+                "us_per_gemv": us, "GBps": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
+                "isolated_us": iso, "isolated_GBps": nbytes / iso / 1e3,
+                "spot_check_max_abs": err}
+
+    shapes = []
+    for m, k, b in SWEEP_SHAPES:
+        per = gemv_bytes(m, k, b)
+        nsets = max(4, -(-3 * L2_BYTES // per))  # > 3x L2 of distinct weights
+        pk, sc, xs, ys = make_stack(torch, quantize, dev, m, k, b, nsets, 20000 + m + k)
+        # first call of each set, so the check below reads computed outputs
+        for i in range(nsets):
+            capi.check(capi.gemv(pk[i].data_ptr(), sc[i].data_ptr(), xs[i].data_ptr(),
+                                 ys[i].data_ptr(), m, k, b, plain, 0, 0,
+                                 torch.cuda.current_stream().cuda_stream), "dk_w4a16_gemv")
+        torch.cuda.synchronize()
+        shapes.append(entry(m, k, b, pk, sc, xs, ys))
+        del pk, sc, xs, ys
+        torch.cuda.empty_cache()
+    batches = []
+    m, k = packed[0].shape[0], packed[0].shape[1] * 8
+    for b in SWEEP_BATCHES:
+        g = torch.Generator(device=dev).manual_seed(30000 + b)
+        xs = [torch.randn(b, k, generator=g, device=dev).half() for _ in packed]
+        ys = [torch.empty(b, m, dtype=torch.float16, device=dev) for _ in packed]
+        capi.check(capi.gemv(packed[0].data_ptr(), scales[0].data_ptr(), xs[0].data_ptr(),
+                             ys[0].data_ptr(), m, k, b, plain, 0, 0,
+                             torch.cuda.current_stream().cuda_stream), "dk_w4a16_gemv")
+        torch.cuda.synchronize()
+        batches.append(entry(m, k, b, packed, scales, xs, ys))
+        del xs, ys
+    return {"protocol": f"chain: {steps} replays of a CUDA graph of one GEMV per distinct weight "
+                        f"set (> 3x L2 of weights, PDL); isolated: 512 MiB fill flush, events "
+                        f"around one plain C-ABI call, median of 100",
+            "shapes": shapes, "batch_sweep_4096x4096": batches}
+
+
+def tp_leg(args, workload: str, ws: int, rank: int, dev, dist, steps: int,
+           check: bool = True) -> dict:
+    """One decode step of ``layers`` decoder layers' projections in the
+    tensor-parallel layout over the ranks (q/k/v and gate/up+SiLU-mul split
+    by output rows with no exchange; o and down K-parallel with the fused
+    reduction: two exchanges per layer), captured in a CUDA graph and
+    replayed ``steps`` times; time = max over ranks.  Every rank takes the
+    same collective steps.  Before timing, rank 0 checks layer 0's outputs:
+    bit for bit against the rank-ordered fp32 sum of the K-slice partials
+    computed on one GPU (the exchange's contract), and within 1e-2 of the
+    unsharded single-GPU GEMVs."""
+    import torch
+
+    import decode_kernel as dk
+    from decode_kernel import capi
+    from decode_kernel.quantize import quantize_and_pack_cuda
+    from decode_kernel.sharded import (PeerBuffers, TensorParallelAttentionProj,
+                                       TensorParallelMLP, split_dim)
+
+    B = args.batch
+    layers = args.layers or (32 if workload == "llama7b-tp" else 8)
+    H, Q, KV, I = tp_layer_shapes(workload)
+    peers = PeerBuffers(8 * ws * B * H)
+
+    def mat(m, k, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)  # same weights on every rank
+        w = torch.randn(m, k, generator=g, device=dev) * 0.02
+        out = quantize_and_pack_cuda(w)
+        del w
+        return out
+
+    blocks, full0 = [], None
+    for layer in range(layers):
+        s0 = 9000 + 10 * layer
+        mats = [mat(Q, H, s0), mat(KV, H, s0 + 1), mat(KV, H, s0 + 2), mat(H, Q, s0 + 3),
+                mat(I, H, s0 + 4), mat(I, H, s0 + 5), mat(H, I, s0 + 6)]
+        attn = TensorParallelAttentionProj(*mats[:4], peers, max_batch=B, exchange=args.exchange)
+        mlp = TensorParallelMLP(*mats[4:], peers, max_batch=B, exchange=args.exchange)
+        blocks.append((attn, mlp))
+        if layer == 0 and check and rank == 0:
+            full0 = mats
+        del mats
+        torch.cuda.empty_cache()
+    x = torch.randn(B, H, generator=torch.Generator(device=dev).manual_seed(1), device=dev).half()
+    # This rank's algorithmic bytes per layer: its weight slices, x per kernel,
+    # the local outputs, and the partials it exchanges.
+    _, nq = split_dim(Q, ws, rank)
+    _, nkv = split_dim(KV, ws, rank)
+    _, ni = split_dim(I, ws, rank)
+    per_layer = (gemv_bytes(nq + 2 * nkv, H, B) + gemv_bytes(H, nq, B) + gemv_bytes(2 * ni, H, B)
+                 - B * ni * 2 + gemv_bytes(H, ni, B))
+    if ws > 1 and args.exchange == "fused":
+        per_layer += 2 * (ws - 1) * B * H * 4
+    shard_bytes = per_layer * layers
+    pdl = not args.no_pdl and args.exchange == "fused"
+    # this library's kernels per layer: q/k/v, o (+ sum), gate/up, down (+ sum)
+    launches = layers * (4 + (2 if ws > 1 and args.exchange == "fused" else 0))
+
+    def step():
+        for attn, mlp in blocks:
+            attn(x, pdl=pdl)
+            mlp(x, pdl=pdl)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    parity = None
+    if check:
+        attn0, mlp0 = blocks[0]
+        ya = attn0(x).clone()
+        ym = mlp0(x).clone()
+        torch.cuda.synchronize()
+        if rank == 0:
+            (pq, sq), _, _, (po, so), (pg, sg), (pu, su), (pd, sd) = full0
+            f32 = capi.default_config(version=5, flags=capi.DK_FLAG_F32_OUT)
+            st = torch.cuda.current_stream().cuda_stream
+
+            def rank_ordered(pw, sw, inp):
+                n = inp.shape[1]
+                acc = torch.zeros((B, pw.shape[0]), dtype=torch.float32, device=dev)
+                for r in range(ws):
+                    k0, kn = split_dim(n, ws, r)
+                    p_r = pw[:, k0 // 8:(k0 + kn) // 8].contiguous()
+                    s_r = sw[:, k0 // 128:(k0 + kn) // 128].contiguous()
+                    x_r = inp[:, k0:k0 + kn].contiguous()
+                    part = torch.empty_like(acc)
+                    capi.check(capi.gemv(p_r.data_ptr(), s_r.data_ptr(), x_r.data_ptr(),
+                                         part.data_ptr(), pw.shape[0], kn, B, f32, 0, 0, st),
+                               "dk_w4a16_gemv")
+                    acc = acc + part
+                return acc.half()
+
+            q = dk.gemv(pq, sq, x)
+            h = dk.gemv_silu_mul((pg, sg), (pu, su), x)
+            want_a, want_m = rank_ordered(po, so, q), rank_ordered(pd, sd, h)
+            parity = {
+                "bitwise_o": bool(torch.equal(ya, want_a)),
+                "bitwise_down": bool(torch.equal(ym, want_m)),
+                "max_abs_vs_unsharded_o": float((ya.float() - dk.gemv(po, so, q).float())
+                                                .abs().max()),
+                "max_abs_vs_unsharded_down": float((ym.float() - dk.gemv(pd, sd, h).float())
+                                                   .abs().max()),
+                "contract": "bit for bit the rank-ordered fp32 sum of the K-slice partials "
+                            "computed on one GPU; within 1e-2 of the unsharded GEMV"}
+            full0 = None
+    # Every rank learns whether rank 0's check passed before anything is timed.
+    ok = torch.tensor([1.0 if parity is None or (
+        parity["bitwise_o"] and parity["bitwise_down"] and
+        parity["max_abs_vs_unsharded_o"] < 1e-2 and parity["max_abs_vs_unsharded_down"] < 1e-2)
+        else 0.0], device=dev)
+    if dist:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if ok.item() != 1.0:
+        raise AssertionError(f"tensor-parallel parity check failed: {parity}")
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clocks:
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    total = torch.tensor([float(shard_bytes)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(total)
+    err = capi.load().dk_device_error(-1, 0)
+    del graph
+    torch.cuda.synchronize()
+    peers.close()
+    ms_max = float(t[0].item())
+    return {"workload": f"{workload} x{layers} layers (hidden {H}, q {Q}, k/v {KV}, "
+                        f"intermediate {I}), B={B}; attention not run",
+            "n_gpus": ws, "steps": steps, "us_per_step": ms_max * 1e3 / steps,
+            "aggregate_GBps": float(total.item()) * steps / (ms_max / 1e3) / 1e9,
+            "exchange": args.exchange, "pdl": pdl,
+            "parallelism": f"tensor-parallel x{ws}: 2 exchanges per layer",
+            "gpu_launches": launches * steps, "device_error": err, "parity": parity,
+            "clocks": clocks.summary(), "layers": layers, "H": H, "Q": Q, "KV": KV, "I": I}
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -541,6 +860,9 @@ def run_ours(args) -> None:
 
         import torch.distributed as dist
 
+        # The exchange is plain peer stores; NCCL carries only barriers and the
+        # max-over-ranks of the timings, with NVLink SHARP (NVLS) off.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
         pg = dist
@@ -708,12 +1030,26 @@ def run_ours(args) -> None:
                          f"dequantize then fp32 BLAS matmul (numpy restatement of "
                          f"reference.py:17-26)"}
 
+    peak, peak_kind = measured_peaks()
+    # The other BASELINE configurations (one GPU, rank 0): extra keys.
+    sweeps = None
+    if rank == 0 and ws == 1 and not args.no_sweeps:
+        del hx, hy, dx, dy
+        sweeps = run_sweeps(args, torch, capi, quantize_and_pack_cuda, dev, packed, scales, peak)
+    # Strong scaling: the 70B-shaped layers sharded over every rank of this
+    # run (the same command at N = 1), with the exchange between the GPUs
+    # and an in-run parity check against the unsharded layer.
+    strong = None
+    if not args.no_strong:
+        del packed, scales, xs, ys
+        torch.cuda.empty_cache()
+        strong = tp_leg(args, "llama70b-tp", ws, rank, dev, pg, max(args.steps, 100))
+
     if pg:
         pg.barrier()
         pg.destroy_process_group()
     if rank != 0:
         return
-    peak, peak_kind = measured_peaks()
     traffic = ncu_traffic_per_launch(M, K, B)
     clk = clocks.summary()
     line = {
@@ -732,17 +1068,10 @@ def run_ours(args) -> None:
         "vs_baseline": None,
         "dtype": "int4*f16->f32",
         "data": "synthetic",
-        "config": {
-            "workload": f"{M}x{K} W4A16 GEMV B={B}",
-            "M": M, "K": K, "global_batch": B * ws,
-            "gemvs_per_step": S,
-            "weight_stack_bytes": S * M * K // 2,
-            "l2": f"inputs larger than L2: {S} distinct weight sets "
-                  f"({S * per_gemv / 2**20:.0f} MiB) cycled, no flush",
-            "kernel": "k_stream (v5), PDL" if not args.no_pdl else "k_stream (v5)",
-            "launch": "CUDA graph of one step, replayed",
-            "parallelism": f"weak x{ws}: independent weight stacks per GPU, no collective",
-        },
+        "config": workload_config(M, K, B, S, ws),
+        "arm": {"kernel": kernel_path(M, K, B) + (", PDL" if not args.no_pdl else ""),
+                "launch": "CUDA graph of one step (one C-ABI call per weight set), replayed",
+                "weight_stack_bytes": S * M * K // 2},
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
@@ -769,6 +1098,10 @@ def run_ours(args) -> None:
         line["isolated"] = isolated
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if sweeps is not None:
+        line["baseline_configs"] = sweeps
+    if strong is not None:
+        line["strong_scaling"] = strong
     line["meta"] = run_meta(local)
     print(json.dumps(line), flush=True)
 
@@ -912,10 +1245,6 @@ def run_tensor_parallel(args) -> None:
 
     import torch
 
-    from decode_kernel.quantize import quantize_and_pack_cuda
-    from decode_kernel.sharded import (PeerBuffers, TensorParallelAttentionProj,
-                                       TensorParallelMLP, split_dim)
-
     ws, rank, local = dist_info()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -924,97 +1253,24 @@ def run_tensor_parallel(args) -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    B = args.batch
-    layers = args.layers or (32 if args.workload == "llama7b-tp" else 8)
-    H, Q, KV, I = tp_layer_shapes(args.workload)
-    peers = PeerBuffers(8 * ws * B * H)
-
-    def mat(m, k, seed):
-        g = torch.Generator(device=dev).manual_seed(seed)  # same weights on every rank
-        w = torch.randn(m, k, generator=g, device=dev) * 0.02
-        out = quantize_and_pack_cuda(w)
-        del w
-        return out
-
-    blocks = []
-    for layer in range(layers):
-        s0 = 9000 + 10 * layer
-        attn = TensorParallelAttentionProj(mat(Q, H, s0), mat(KV, H, s0 + 1), mat(KV, H, s0 + 2),
-                                           mat(H, Q, s0 + 3), peers, max_batch=B,
-                                           exchange=args.exchange)
-        mlp = TensorParallelMLP(mat(I, H, s0 + 4), mat(I, H, s0 + 5), mat(H, I, s0 + 6), peers,
-                                max_batch=B, exchange=args.exchange)
-        blocks.append((attn, mlp))
-        torch.cuda.empty_cache()
-    x = torch.randn(B, H, generator=torch.Generator(device=dev).manual_seed(1), device=dev).half()
-    # This rank's algorithmic bytes per layer: its weight slices, x per kernel,
-    # the local outputs, and the partials it exchanges.
-    _, nq = split_dim(Q, ws, rank)
-    _, nkv = split_dim(KV, ws, rank)
-    _, ni = split_dim(I, ws, rank)
-    per_layer = (gemv_bytes(nq + 2 * nkv, H, B) + gemv_bytes(H, nq, B) + gemv_bytes(2 * ni, H, B)
-                 - B * ni * 2 + gemv_bytes(H, ni, B))
-    if ws > 1 and args.exchange == "fused":
-        per_layer += 2 * (ws - 1) * B * H * 4
-    shard_bytes = per_layer * layers
-    pdl = not args.no_pdl and args.exchange == "fused"
-    # this library's kernels per layer: q/k/v, o (+ sum), gate/up, down (+ sum)
-    launches = layers * (4 + (2 if ws > 1 and args.exchange == "fused" else 0))
-
-    def step():
-        for attn, mlp in blocks:
-            attn(x, pdl=pdl)
-            mlp(x, pdl=pdl)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    graph.replay()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        e0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    total = torch.tensor([float(shard_bytes)], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(total)
-    from decode_kernel import capi
-
-    err = capi.load().dk_device_error(-1, 0)
-    del graph
-    torch.cuda.synchronize()
-    peers.close()
+    leg = tp_leg(args, args.workload, ws, rank, dev, dist, args.steps)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    ms_max = float(t[0].item())
-    value = float(total.item()) * args.steps / (ms_max / 1e3) / 1e9
     line = {
         "metric": f"aggregate HBM read GB/s, {args.workload} decode-step projections",
-        "value": value, "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "us_per_token": ms_max * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4*f16->f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload} x{layers} layers (hidden {H}, q {Q}, k/v {KV}, "
-                               f"intermediate {I}), B={B}; attention not run",
-                   "global_batch": B, "exchange": args.exchange, "pdl": pdl,
-                   "parallelism": f"tensor-parallel x{ws}: 2 exchanges per layer",
+        "value": leg["aggregate_GBps"], "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": leg["us_per_step"] / 1e3,
+        "us_per_token": leg["us_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int4*f16->f32", "data": "synthetic",
+        "config": {"workload": leg["workload"], "global_batch": args.batch,
+                   "exchange": args.exchange, "pdl": leg["pdl"],
+                   "parallelism": leg["parallelism"],
                    "l2": "inputs larger than L2 (the step streams every layer's weights)"},
-        "device_error": err, "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
+        "device_error": leg["device_error"], "parity": leg["parity"],
+        "gpu_launches": leg["gpu_launches"], "clocks": leg["clocks"],
     }
     line["meta"] = run_meta(local)
     print(json.dumps(line), flush=True)
@@ -1047,6 +1303,10 @@ def main() -> None:
                          "the ranks); llama7b-tp / llama70b-tp: the same layers in the "
                          "tensor-parallel layout, two exchanges per layer")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--no-sweeps", action="store_true",
+                    help="skip the other BASELINE configs (shapes, batch sweep)")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong-scaling leg (70B-shaped tensor-parallel layers)")
     ap.add_argument("--layers", type=int, default=0)
     args = ap.parse_args()
     if args.warmup < 3:

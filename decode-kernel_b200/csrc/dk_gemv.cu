@@ -1175,6 +1175,30 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
 constexpr int kStampReuse = 15;
 constexpr int kMaxBatchPerPass = 32;  // 4 mma n-tiles
 
+// Host half of the dispatch stamp.  The reference clears the device stamp to
+// -1 with a copy before every launch (gemv_w4a16.cu:553-557), so a call that
+// launches nothing leaves -1 behind.  A copy on the caller's stream would sit
+// between two PDL-chained GEMVs and serialise them, so here every GEMV entry
+// point marks its device "nothing launched" on entry and "launched" once a
+// kernel launch has succeeded; dk_last_kernel_stamp reports -1 while the mark
+// says nothing was launched, and the stamp the kernel wrote otherwise.
+constexpr int kStampDevices = 64;
+std::atomic<int> g_stamp_live[kStampDevices];
+
+void stamp_begin_call() {
+  const int dev = current_device();
+  if (dev >= 0 && dev < kStampDevices) g_stamp_live[dev].store(0, std::memory_order_relaxed);
+}
+
+void stamp_launched() {
+  const int dev = current_device();
+  if (dev >= 0 && dev < kStampDevices) g_stamp_live[dev].store(1, std::memory_order_relaxed);
+}
+
+bool stamp_is_live(int dev) {
+  return dev >= 0 && dev < kStampDevices && g_stamp_live[dev].load(std::memory_order_relaxed);
+}
+
 template <typename Kern, typename... Args>
 dk_status launch(const char* name, Kern kernel, dim3 grid, dim3 block, size_t smem,
                  cudaStream_t stream, bool pdl, Args... args) {
@@ -1195,6 +1219,7 @@ dk_status launch(const char* name, Kern kernel, dim3 grid, dim3 block, size_t sm
     set_cuda_error(e, name);
     return DK_ERR_LAUNCH;
   }
+  stamp_launched();
   return DK_OK;
 }
 
@@ -1467,6 +1492,7 @@ extern "C" dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales
                                    const uint16_t* x, uint16_t* y, int M, int K, int B,
                                    const dk_gemv_config* cfg, void* workspace,
                                    size_t workspace_bytes, void* stream) {
+  stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
   if (cfg) c = *cfg;
@@ -1573,6 +1599,7 @@ extern "C" dk_status dk_w4a16_gemv_multi(int n, const int32_t* const* packed,
                                          const uint16_t* const* scales, const int* M,
                                          uint16_t* const* y, const uint16_t* x, int K, int B,
                                          const dk_gemv_config* cfg, void* stream) {
+  stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
   if (cfg) c = *cfg;
@@ -1645,6 +1672,7 @@ extern "C" dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate,
                                             const int32_t* packed_up, const uint16_t* scales_up,
                                             const uint16_t* x, uint16_t* h, int M, int K, int B,
                                             const dk_gemv_config* cfg, void* stream) {
+  stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
   if (cfg) c = *cfg;
@@ -1709,6 +1737,7 @@ static int shard_grid(int rows) { return std::max(1, std::min(sm_count(-1), (row
 
 static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_gemv_config* cfg,
                               cudaStream_t st) {
+  stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
   if (cfg) c = *cfg;
@@ -1751,6 +1780,7 @@ extern "C" dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_
                                             int M_total, int K, int B,
                                             const dk_shard_group* group,
                                             const dk_gemv_config* cfg, void* stream) {
+  stamp_begin_call();
   if (M_shard <= 0 || row0 < 0 || M_total < row0 + M_shard) return DK_ERR_INVALID_ARG;
   GemvParams p;
   p.packed = reinterpret_cast<const uint32_t*>(packed);
@@ -1827,6 +1857,7 @@ static void* noalloc_scratch_ptr(dk_status* st) {
 extern "C" dk_status dk_w4a16_gemv_splitk_noalloc(const int32_t* packed, const uint16_t* scales,
                                                   const uint16_t* x, uint16_t* y, int M, int K,
                                                   int B, int split_k, void* stream) {
+  stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
   c.version = 4;
@@ -1853,7 +1884,9 @@ extern "C" int dk_last_kernel_stamp(int device) {
   if (device >= 0 && device != prev) cudaSetDevice(device);
   int h = -1;
   cudaDeviceSynchronize();
-  if (cudaMemcpyFromSymbol(&h, g_dk_kernel_stamp, sizeof(int)) != cudaSuccess) h = -1;
+  if (!stamp_is_live(current_device()) ||
+      cudaMemcpyFromSymbol(&h, g_dk_kernel_stamp, sizeof(int)) != cudaSuccess)
+    h = -1;
   if (device >= 0 && device != prev) cudaSetDevice(prev);
   return h;
 }

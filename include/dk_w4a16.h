@@ -126,10 +126,16 @@ DK_API dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales, co
  * until the process exits; the caller passes only inputs and outputs.
  *  - Problems whose split-K workspace (dk_w4a16_workspace_bytes with
  *    version 4) exceeds the buffer return DK_ERR_WORKSPACE.  Batches run in
- *    passes of 8 rows, so the limit is M * (K/128) * 4 bytes plus a few KB of
- *    counters for B >= 8 (e.g. M * K <= ~250M weights at B = 1).
+ *    passes of up to 8 rows, so the need is the arrival counters
+ *    (ceil(M/16) * 4 bytes, rounded up to 256) plus M * (K/128) * min(B, 8)
+ *    * 4 bytes: about M * K <= 268M weights at B = 1, and M * K <= 33M
+ *    weights at B >= 8 (4096 x 8176 fits, 4096 x 8192 does not).  A split
+ *    that clamps to 1 (K = 128) needs no scratch at all.
  *  - The first call on a device looks up the buffer's device address with that
- *    device current; make that first call before any stream capture.
+ *    device current; make that first call before any stream capture.  The
+ *    address is kept for the life of the process: the library must not be
+ *    used across a cudaDeviceReset (or any destruction of the device's
+ *    primary context), which may reload the module elsewhere.
  *  - All calls share the one buffer per device: calls that can overlap on the
  *    GPU (different streams without ordering) race and must not be issued.
  *    Each call clears what has to start at zero.
@@ -181,6 +187,19 @@ DK_API dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate, const uint16
  * the sum polls the words themselves (no slots, no separate wait).  All
  * ranks must run on the same GPU model (the grid is derived from the shape
  * and the SM count).
+ *
+ * Two buffer sets, used in turn.  A rank that has finished call e may store
+ * call e+1's results into a slower rank's buffer while that rank still reads
+ * call e's gathered result, and a K-parallel word of call e+1 may replace
+ * the call-e word before that rank's sum has read it (that sum then waits
+ * until its bound runs out).  So every rank keeps two sets of `bufs` (and
+ * two dk_shard_group values that differ only in `bufs`; `slots` and `seq`
+ * are shared) and consecutive sharded calls alternate between them: set
+ * e % 2 for call e.  A set may be written again only by call e+2, i.e.
+ * after this rank's wait (dk_shard_wait, DK_FLAG_SHARD_WAIT) or sum
+ * (dk_shard_reduce) of call e+1 -- which cannot complete before every rank
+ * has finished reading call e's set.  decode_kernel.sharded.PeerBuffers
+ * keeps the two sets and alternates them (PeerBuffers.begin()).
  * ------------------------------------------------------------------------ */
 #define DK_MAX_SHARDS 8
 #define DK_SHARD_SLOTS 256 /* arrival slots per rank and call, >= any grid */
@@ -260,7 +279,11 @@ DK_API int dk_stream_recommended_blocks(int device);
 
 /* Stamp written by the GEMV kernel that ran last on `device` (-1 = current):
  * 0..5 for versions 0..5, 10+w for version 1 with w>1 warps per row, 15 for
- * the batch weight-reuse path; -1 if none has run.  Synchronises the device
+ * the batch weight-reuse path; -1 if none has run, and -1 when the last GEMV
+ * call on that device launched nothing (arguments rejected, empty problem,
+ * failed launch) -- the result of the reference's reset of the stamp before
+ * every launch (gemv_w4a16.cu:553-557), kept here on the host so that no copy
+ * sits between PDL-chained GEMVs on the stream.  Synchronises the device
  * first, like gemv_w4a16.cu:559-564. */
 DK_API int dk_last_kernel_stamp(int device);
 

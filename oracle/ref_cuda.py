@@ -21,8 +21,9 @@ from pathlib import Path
 
 _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "_ref" / "libdkref.so"
-# The reference checkout; DK_REFERENCE overrides it, as for tests/golden/make_golden.py.
-REF_CHECKOUT = Path(os.environ.get("DK_REFERENCE", "/root/reference"))
+# The reference checkout: DK_REFERENCE, as for tests/golden/make_golden.py, else
+# a checkout named "reference" beside this repository.
+REF_CHECKOUT = Path(os.environ.get("DK_REFERENCE") or (_HERE.parent.parent / "reference"))
 _lib = None
 
 

@@ -48,6 +48,11 @@ def test_reference_arm_line_on_host_cores():
     assert d["value"] > 0 and d["unit"] == "GB/s" and d["higher_is_better"] is True
     assert d["steps"] == 2 and d["warmup"] == 3 and d["n_gpus"] == 1
     assert d["config"]["workload"] == "512x1024 W4A16 GEMV B=1"
+    # The same workload dict this library's arm reports (bench.workload_config).
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    assert d["config"] == bench.workload_config(512, 1024, 1, 64, 1)
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
@@ -62,6 +67,16 @@ def test_reference_arm_other_ranks_exit_quietly():
                "--no-reference-cuda", env={"WORLD_SIZE": "2", "RANK": "1", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_kernel_path_follows_the_dispatch():
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    assert bench.kernel_path(4096, 4096, 1).startswith("k_stream (v5, 1 n-tile")
+    assert bench.kernel_path(4096, 4096, 16).startswith("k_stream (v5, 2 n-tiles")
+    assert bench.kernel_path(4096, 4096, 32).startswith("k_stream (v5, 4 n-tiles")
+    assert bench.kernel_path(28672, 8192, 32) == "k_batch (tcgen05)"
 
 
 def test_run_meta_never_raises_without_a_gpu():

@@ -82,6 +82,32 @@ def test_warps_per_row(wpr, cuda_device):
     assert stamp() == (1 if wpr == 1 else 10 + wpr)
 
 
+def test_stamp_resets_when_a_call_launches_nothing(cuda_device):
+    # The reference clears the stamp before every launch (gemv_w4a16.cu:553-557),
+    # so after a call that ran no kernel last_kernel_stamp is -1, not the
+    # stamp of the kernel before it.
+    from decode_kernel import capi
+
+    lib = capi.load()
+    packed, scales, x = make_problem(64, 256, 1, seed=4)
+    tp, ts, tx = to_device(packed, scales, x)
+    capi_gemv(tp, ts, tx, cfg(version=3))
+    assert stamp() == 3
+    y = torch.empty(1, 64, dtype=torch.float16, device=cuda_device)
+    bad = cfg(version=3)
+    st = capi.gemv(tp.data_ptr(), ts.data_ptr(), tx.data_ptr() + 2, y.data_ptr(), 64, 256, 1, bad,
+                   0, 0, torch.cuda.current_stream().cuda_stream)  # misaligned x: rejected
+    assert st == capi.DK_ERR_INVALID_ARG
+    assert stamp() == -1
+    capi_gemv(tp, ts, tx, cfg(version=2))
+    assert stamp() == 2
+    st = capi.gemv(tp.data_ptr(), ts.data_ptr(), tx.data_ptr(), y.data_ptr(), 0, 256, 1, bad, 0,
+                   0, torch.cuda.current_stream().cuda_stream)  # M = 0: nothing to launch
+    assert st == capi.DK_OK
+    assert stamp() == -1
+    assert lib.dk_last_kernel_stamp(-1) == -1
+
+
 def test_tensor_core_family_is_bitwise_identical(cuda_device):
     M, K, B = 777, 11008, 5
     packed, scales, x = make_problem(M, K, B, seed=11)

@@ -67,3 +67,35 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
         assert torch.equal(got, want)  # same kernel, same reduction order
         assert max_err(got, oracle_y(x, packed, scales)) < MAX_ABS
     assert capi.load().dk_device_error(-1, 0) == 0
+
+
+# (M, K, B, split): batches that run in one pass (B = 1) and in several 8-row
+# passes that reuse the shared buffer on one stream (B = 9, 17); a problem
+# whose scratch (counters + 8 rows of per-group partials) reaches to within
+# 15 KB of the buffer's end; K = 128, where the split clamps to 1 and no
+# scratch is used at all.
+NOALLOC_CASES = [(1000, 4096, 1, 4), (1000, 4096, 9, 4), (600, 2048, 17, 8),
+                 (8176, 4096, 9, 4), (300, 128, 17, 4)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,B,split", NOALLOC_CASES)
+def test_noalloc_batches_and_limits(M, K, B, split, cuda_device):
+    import torch
+    from decode_kernel import capi
+
+    cfg4 = capi.default_config(version=4, split_k=split)
+    need = capi.workspace_bytes(M, K, B, cfg4)
+    assert need <= capi.DK_NOALLOC_SCRATCH_BYTES
+    if K == 128:
+        assert need == 0
+    packed, scales, x = make_problem(M, K, B, seed=M + K + B)
+    tp, ts, tx = to_device(packed, scales, x)
+    want = capi_gemv(tp, ts, tx, cfg4)
+    for call in range(2):
+        got = torch.full((B, M), float("nan"), dtype=torch.float16, device=cuda_device)
+        capi.check(_noalloc(tp, ts, tx, got, split), f"noalloc call {call}")
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), call
+    assert max_err(got, oracle_y(x, packed, scales)) < MAX_ABS
+    assert capi.load().dk_device_error(-1, 0) == 0
