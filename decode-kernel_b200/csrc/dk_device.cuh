@@ -316,6 +316,28 @@ __device__ __forceinline__ bool mbar_wait_spin_bounded(uint64_t* bar, uint32_t p
   }
 }
 
+// Same bound, polling with the non-suspending test and a short sleep between
+// tests: for a wait whose end is latency-critical (a suspended warp resumes
+// late) but that should still leave most issue slots to the other warps of
+// its sub-partition.
+__device__ __forceinline__ bool mbar_wait_poll_bounded(uint64_t* bar, uint32_t parity,
+                                                       volatile int* abort_flag) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = 0;; ++i) {
+    __nanosleep(32);
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 63) == 63) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(&g_dk_device_error, kDevWaitTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -36,6 +36,7 @@
 // the instruction budget per weight is ~1.3 (9 for the unpack of 8 weights),
 // well under the ~2.6 B200 can issue per weight at HBM speed.
 #include <algorithm>
+#include <type_traits>
 #include <atomic>
 #include <cstdio>
 #include <cstring>
@@ -47,6 +48,7 @@
 #define DK_DEVICE_GLOBALS
 #include "dk_device.cuh"
 #include "dk_host.h"
+
 
 namespace dk {
 
@@ -109,10 +111,12 @@ struct GemvParams {
   OutSpec out;             // v5: destination of y
 };
 
-// A CTA's share of a v5 call and its 16-row tiles.  One matrix: rows
-// [r0, r1) = [bid·M/grid, (bid+1)·M/grid) (the last tile may be partial).
-// Several matrices: whole global tiles [t0, t0 + ntiles) of the segments'
-// concatenation, each inside one segment.
+// A CTA's share of a v5 call: whole 16-row tiles, so no CTA fetches or
+// computes rows of its neighbour.  One matrix: tiles [t0, t0 + ntiles) =
+// [bid·T/grid, (bid+1)·T/grid) of the T = ceil(M/16) tiles, rows [r0, r1)
+// (only the matrix's last tile may be partial).  Several matrices: whole
+// global tiles [t0, t0 + ntiles) of the segments' concatenation, each inside
+// one segment.
 struct TileRef {
   int seg, row, rows;  // segment, first row inside it, valid rows
 };
@@ -141,10 +145,11 @@ struct CtaTiles {
   int ntiles;
   __device__ __forceinline__ void init(const GemvParams& p, const StreamArgs<MULTI>& a) {
     if constexpr (!MULTI) {
-      r0 = (int)(((long long)blockIdx.x * p.M) / gridDim.x);
-      r1 = (int)(((long long)(blockIdx.x + 1) * p.M) / gridDim.x);
-      t0 = 0;
-      ntiles = (r1 - r0 + 15) / 16;
+      const int T = (p.M + 15) / 16;
+      t0 = (int)(((long long)blockIdx.x * T) / gridDim.x);
+      ntiles = (int)(((long long)(blockIdx.x + 1) * T) / gridDim.x) - t0;
+      r0 = t0 * 16;
+      r1 = min(p.M, (t0 + ntiles) * 16);
     } else {
       const int ntot = a.segs.units();
       t0 = (int)(((long long)blockIdx.x * ntot) / gridDim.x);
@@ -259,9 +264,11 @@ __device__ __forceinline__ void load_x_group(const __half* __restrict__ x, int K
 // One group (128 k) of a 16-row tile: thread (g, c) holds words 4c..4c+3 of
 // the group for rows g (wa) and g+8 (wb).  Eight HMMAs; the quad's four
 // threads supply the 16 k of each one, all inside this group, so the group
-// scale can be applied to the fp32 result afterwards.  The eight form two
-// independent accumulation chains (words 0-1 and words 2-3) that are added at
-// the end: D_G = chain01 + chain23.  Every kernel computes D_G this way.
+// scale can be applied to the fp32 result afterwards.  The eight run as one
+// accumulation chain from zero, word t = 0..3 in order and each word's two
+// MMAs in order: that chain is D_G, and every kernel computes it this way.
+// (Two chains joined by an add cost one more fp32 add per output per group;
+// ILP comes from the independent groups and warps instead.)
 __device__ __forceinline__ void word_mma(float (&d)[4], uint32_t wa, uint32_t wb,
                                          const uint32_t (&px)[4]) {
   uint32_t ha[4], hb[4];
@@ -271,11 +278,6 @@ __device__ __forceinline__ void word_mma(float (&d)[4], uint32_t wa, uint32_t wb
   mma16816(d, ha[2], hb[2], ha[3], hb[3], px[2], px[3]);
 }
 
-__device__ __forceinline__ void join_chains(float (&d)[4], const float (&e)[4]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) d[i] = __fadd_rn(d[i], e[i]);
-}
-
 template <int NT>
 __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb,
                                           const uint4 (&xr)[NT][4], float (&d)[NT][4]) {
@@ -283,27 +285,24 @@ __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb,
   const uint32_t Bw[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    float e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       uint32_t px[4];
       pair_x8(xr[nt][t], px);
-      if (t < 2)
-        word_mma(d[nt], A[t], Bw[t], px);
-      else
-        word_mma(e, A[t], Bw[t], px);
+      word_mma(d[nt], A[t], Bw[t], px);
     }
-    join_chains(d[nt], e);
   }
 }
 
 // Canonical reduction order, shared by v2, v3, v4, v5 and the reuse path so
 // that all of them return the same bits for the same inputs (and y[b] does
 // not depend on which other batch rows or output rows are in the call):
-//   a_G      = fp32(scale[m, G] * D_G)   (D_G: the group's HMMA dot product)
-//   acc_w    = (((0 + a_w) + a_{w+16}) + a_{w+32}) + ...   for w = 0..15
+//   acc_w    = fma(s_G, D_G, acc_w) for G = w, w+16, w+32, ... (from 0),
+//              w = 0..15; s_G = scale[m, G] in fp32, D_G the group's HMMA
+//              chain; one fp32 rounding per group (fused multiply-add)
 //   y        = fp16_rn((((0 + acc_0) + acc_1) + ...) + acc_15)
-// Explicit _rn intrinsics keep the compiler from contracting mul+add.
+// fmaf is always fused and the sums use _rn intrinsics, so the compiler can
+// neither split the one nor contract the other.
 constexpr int kClasses = 16;
 
 template <int NT>
@@ -311,10 +310,10 @@ __device__ __forceinline__ void scale_accumulate(float (&acc)[NT][4], const floa
                                                  float sa, float sb) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    acc[nt][0] = __fadd_rn(acc[nt][0], __fmul_rn(sa, d[nt][0]));
-    acc[nt][1] = __fadd_rn(acc[nt][1], __fmul_rn(sa, d[nt][1]));
-    acc[nt][2] = __fadd_rn(acc[nt][2], __fmul_rn(sb, d[nt][2]));
-    acc[nt][3] = __fadd_rn(acc[nt][3], __fmul_rn(sb, d[nt][3]));
+    acc[nt][0] = fmaf(sa, d[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(sa, d[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(sb, d[nt][2], acc[nt][2]);
+    acc[nt][3] = fmaf(sb, d[nt][3], acc[nt][3]);
   }
 }
 
@@ -458,10 +457,10 @@ enum TileMode { kTileDirect = 0, kTileScales = 1, kTileSplitK = 2 };
 constexpr int kTileWarps = 8;
 constexpr int kTilePrefetch = 4;
 
-// Split-K finish: every CTA has stored its groups' products a_G in the
+// Split-K finish: every CTA has stored its groups' HMMA chains D_G in the
 // workspace ([groups][B][M] fp32); the last CTA of the tile to arrive replays
-// the canonical order over all groups, so y is bit-identical to v2/v3/v5 for
-// any split count.
+// the canonical order over all groups with the scales, so y is bit-identical
+// to v2/v3/v5 for any split count.
 __device__ __forceinline__ void split_k_finish(const GemvParams& p, int rows, int trow,
                                                unsigned* s_last) {
   __threadfence();
@@ -474,12 +473,14 @@ __device__ __forceinline__ void split_k_finish(const GemvParams& p, int rows, in
   for (int o = threadIdx.x; o < 16 * p.B; o += blockDim.x) {
     const int r = o % 16, b = o / 16;
     if (r >= rows) continue;
-    const float* a = p.ws + (size_t)b * p.M + trow + r;
+    const float* dg = p.ws + (size_t)b * p.M + trow + r;
+    const __half* sg = p.scales + (size_t)(trow + r) * groups;
     const size_t gstride = (size_t)p.B * p.M;
     float y = 0.f;
     for (int w = 0; w < kClasses; ++w) {
       float acc = 0.f;
-      for (int G = w; G < groups; G += kClasses) acc = __fadd_rn(acc, __ldcg(a + G * gstride));
+      for (int G = w; G < groups; G += kClasses)
+        acc = fmaf(ldg_half(sg + G), __ldcg(dg + G * gstride), acc);
       y = __fadd_rn(y, acc);
     }
     p.y[(size_t)b * p.M + trow + r] = __float2half_rn(y);
@@ -487,11 +488,10 @@ __device__ __forceinline__ void split_k_finish(const GemvParams& p, int rows, in
   if (threadIdx.x == 0) p.counters[blockIdx.x] = 0u;  // ready for the next call
 }
 
-// Stores a_G = scale * D_G of one group for this thread's rows and columns.
+// Stores D_G, one group's HMMA chain, for this thread's rows and columns.
 template <int NT>
 __device__ __forceinline__ void store_group_products(const GemvParams& p, const float (&d)[NT][4],
-                                                     float sa, float sb, int G, int trow, int rows,
-                                                     int g, int c) {
+                                                     int G, int trow, int rows, int g, int c) {
   float* base = p.ws + (size_t)G * p.B * p.M + trow;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -499,7 +499,7 @@ __device__ __forceinline__ void store_group_products(const GemvParams& p, const 
     for (int j = 0; j < 4; ++j) {
       const int r = (j < 2) ? g : g + 8;
       const int b = nt * 8 + 2 * c + (j & 1);
-      if (r < rows && b < p.B) base[(size_t)b * p.M + r] = __fmul_rn(j < 2 ? sa : sb, d[nt][j]);
+      if (r < rows && b < p.B) base[(size_t)b * p.M + r] = d[nt][j];
     }
   }
 }
@@ -589,7 +589,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
         for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
         group_mma<NT>(ca, cb, xr, d);
         if (MODE == kTileSplitK && gridDim.y > 1)
-          store_group_products<NT>(p, d, sa, sb, G, trow, rows, g, c);
+          store_group_products<NT>(p, d, G, trow, rows, g, c);
         else
           scale_accumulate<NT>(acc[i & 1], d, sa, sb);
       }
@@ -743,28 +743,23 @@ __device__ __forceinline__ uint32_t frag_off(int R, int gi, int c) {
   return R * v5::kPadRowStride + gi * 64 + c * 16;
 }
 
-// One group, B fragments from the rearranged shared copy of x (two chains,
-// same arithmetic as group_mma).
+// One group, B fragments from the rearranged shared copy of x (same chain as
+// group_mma).
 __device__ __forceinline__ void group_mma_xs(const uint4& wa, const uint4& wb, uint32_t xq,
                                              float (&d)[4]) {
   const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t Bw[4] = {wb.x, wb.y, wb.z, wb.w};
-  float e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const uint4 x4 = lds128(xq + 64 * t);
     const uint32_t px[4] = {x4.x, x4.y, x4.z, x4.w};
-    if (t < 2)
-      word_mma(d, A[t], Bw[t], px);
-    else
-      word_mma(e, A[t], Bw[t], px);
+    word_mma(d, A[t], Bw[t], px);
   }
-  join_chains(d, e);
 }
 
 // One group with x read from global memory, for the streaming kernel: the
 // weights are unpacked once and reused for every n-tile, and x is loaded one
-// n-tile at a time (register budget at 544 threads).  Same HMMA chains as
+// n-tile at a time (register budget at 544 threads).  Same HMMA chain as
 // group_mma, so the same bits.
 template <int NT>
 __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
@@ -784,22 +779,19 @@ __device__ __forceinline__ void group_mma_gx(const uint4& wa, const uint4& wb,
     uint4 xr[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) xr[t] = ldg_keep(xb + 8 * t);
-    float e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       uint32_t px[4];
       pair_x8(xr[t], px);
-      float(&acc)[4] = (t < 2) ? d[nt] : e;
-      mma16816(acc, ha[t][0], hb[t][0], ha[t][1], hb[t][1], px[0], px[1]);
-      mma16816(acc, ha[t][2], hb[t][2], ha[t][3], hb[t][3], px[2], px[3]);
+      mma16816(d[nt], ha[t][0], hb[t][0], ha[t][1], hb[t][1], px[0], px[1]);
+      mma16816(d[nt], ha[t][2], hb[t][2], ha[t][3], hb[t][3], px[2], px[3]);
     }
-    join_chains(d[nt], e);
   }
 }
 
 
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW, int SEG>
-__global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
+__global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     k_stream(const __grid_constant__ StreamArgs<SEG != kSegOne> a, GemvParams p) {
   using namespace v5;
   constexpr bool MULTI = SEG != kSegOne;
@@ -861,162 +853,143 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
   pdl_trigger();
 
   if (warp == kConsumerWarps) {
-    // ---------------- producer: weight stages and tile sums ----------------
-    // It never blocks: each pass issues the next stage if its slot is free
-    // and adds up the next tile if all consumer warps have stored it, so the
-    // consumers never wait on a reduction and a pending reduction never
-    // waits on a slot.
+    // ---------------- issuer: weight stages ----------------
+    // It only issues copies, so it waits in bounded blocking waits (a warp
+    // suspended in try_wait takes no issue slots from the consumer warps that
+    // share its sub-partition; a slot comes back only once every consumer warp
+    // has released it, so a starved warp would pace the whole CTA).
     const uint64_t policy = policy_evict_first();
     const size_t row_bytes = (size_t)p.K / 2;
     StageCursor cur;
-    int issued = 0, reduced = 0;
-    uint64_t idle_since = 0;
-    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
-    while (issued < total || reduced < ntiles) {
-      bool progress = false;
-      if (issued < total) {
-        // x is loaded by the consumers while the first stages stream; holding
-        // the rest back until it has landed keeps those loads from queueing
-        // behind a full ring of weight copies.
-        bool go = !(XS && issued == kStagesBeforeX) || warp_test_wait(xready, 0);
-        if (go && issued >= stages) go = warp_test_wait(&empty[cur.slot], (cur.round - 1) & 1);
-        if (go) {
-          const TileRef tr = tiles(a, cur.tile);
-          const CUtensorMap* tmap;
-          const __half* sscales;
-          const uint32_t* spacked;
-          if constexpr (MULTI) {
-            tmap = &a.m[tr.seg];
-            sscales = a.segs.s[tr.seg].scales;
-            spacked = a.segs.s[tr.seg].packed;
-          } else {
-            tmap = &a.m[0];
-            sscales = p.scales;
-            spacked = p.packed;
-          }
-          const int trow = tr.row;
-          const uint32_t dst = ring + cur.slot * kStageBytes;
-          if constexpr (TMAP) {
-            if (lane == 0) {
-              mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
-              tma_load_3d(dst, tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot],
-                          policy);
-            }
-            // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups)
-            // per cp.async.  K % 256 == 0 here, so scale rows are 4-byte
-            // aligned.
-            const uint32_t sdst = scs + cur.slot * kStageScaleBytes;
-            const int gbase = cur.chunk * kChunkGroups;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
-              // (one matrix: rows past this CTA's share are the next CTA's,
-              // in bounds and harmless)
-              if ((MULTI ? r < tr.rows : trow + r < p.M) && gbase + w2 < groups)
-                cp_async4(sdst + r * kScaleRowStride + w2 * 2,
-                          sscales + (size_t)(trow + r) * groups + gbase + w2);
-            }
-            cp_async_mbar_arrive(&full[cur.slot]);
-          } else {
-            const int rows = tr.rows;
-            const uint32_t bytes =
-                (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
-            if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
-            __syncwarp();
-            if (lane < rows) {
-              const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(spacked);
-              bulk_g2s(dst + lane * kPadRowStride,
-                       wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
-                       bytes, &full[cur.slot], policy);
-            }
-          }
-          ++issued;
-          cur.next(nk, stages);
-          progress = true;
-        }
-      }
-      if (reduced < ntiles &&
-          warp_test_wait(&red_full[reduced % kRedBufs], (reduced / kRedBufs) & 1)) {
-        // Tile `reduced`: the 16 class partials of every real row and batch
-        // column, added in class order.
-        const float* rt = red + (reduced % kRedBufs) * kClasses * 16 * nbp;
-        const TileRef tr = tiles(a, reduced);
-        const int trow = tr.row, rows = tr.rows;
-        const int nb = min(W, p.B);
-        if (!MULTI && reduced == 0 && p.out.mode == kOutKShard) {
-          pdl_wait();  // the number was advanced by the previous call's sum
-          tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
-        }
-        constexpr bool paired = SEG == kSegPair;
-        if (paired && tr.seg == 0) {
-          // Gate tile: its partials stay in their buffer until the up tile
-          // of the same rows has been added up too.
-        } else {
-          for (int o = lane; o < rows * nb; o += 32) {
-            const int r = o / nb, b = o - r * nb;
-            const float* src = rt + r * nbp + b;
-            float sum = 0.f;
-#pragma unroll
-            for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
-            if constexpr (MULTI) {
-              if (paired) {
-                // h = silu(g) * u with the roundings of the unfused fp16
-                // sequence: g and u as GEMV outputs, silu(g) = g / (1 +
-                // exp(-g)) in fp32 rounded to fp16, the product in fp32
-                // rounded to fp16.
-                const float* gsrc =
-                    red + ((reduced - 1) % kRedBufs) * kClasses * 16 * nbp + r * nbp + b;
-                float gsum = 0.f;
-#pragma unroll
-                for (int w = 0; w < kClasses; ++w) gsum = __fadd_rn(gsum, gsrc[w * 16 * nbp]);
-                const float g = __half2float(__float2half_rn(gsum));
-                const float sg = __half2float(__float2half_rn(g / (1.0f + expf(-g))));
-                const float u = __half2float(__float2half_rn(sum));
-                const Segment& s0 = a.segs.s[0];
-                s0.y[(size_t)b * s0.rows + trow + r] = __float2half_rn(__fmul_rn(sg, u));
-              } else {
-                const Segment& sg = a.segs.s[tr.seg];
-                sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
-              }
-            } else {
-              store_y(p, b, trow + r, sum, tag);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) {
-            if (paired) mbar_arrive(&red_free[(reduced - 1) % kRedBufs]);
-            mbar_arrive(&red_free[reduced % kRedBufs]);
-          }
-        }
-        ++reduced;
-        progress = true;
-      }
-      if (progress) {
-        idle_since = 0;
+    int issued = 0;
+    for (; issued < total; ++issued) {
+      // x is loaded by the consumers while the first stages stream; holding
+      // the rest back until it has landed keeps those loads from queueing
+      // behind a full ring of weight copies.
+      if (XS && issued == kStagesBeforeX && !mbar_wait_bounded(xready, 0, abort_flag)) break;
+      if (issued >= stages &&
+          !mbar_wait_bounded(&empty[cur.slot], (cur.round - 1) & 1, abort_flag))
+        break;
+      const TileRef tr = tiles(a, cur.tile);
+      const CUtensorMap* tmap;
+      const __half* sscales;
+      const uint32_t* spacked;
+      if constexpr (MULTI) {
+        tmap = &a.m[tr.seg];
+        sscales = a.segs.s[tr.seg].scales;
+        spacked = a.segs.s[tr.seg].packed;
       } else {
-        if (*abort_flag) break;
-        const uint64_t now = globaltimer_ns();
-        if (idle_since == 0) {
-          idle_since = now;
-        } else if (now - idle_since > kWaitLimitNs) {
-          if (lane == 0) atomicExch(&g_dk_device_error, kDevWaitTimeout);
-          *abort_flag = 1;
-          break;
+        tmap = &a.m[0];
+        sscales = p.scales;
+        spacked = p.packed;
+      }
+      const int trow = tr.row;
+      const uint32_t dst = ring + cur.slot * kStageBytes;
+      if constexpr (TMAP) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[cur.slot], (uint32_t)kStageBytes);
+          tma_load_3d(dst, tmap, 0, trow, cur.chunk * kStripsPerChunk, &full[cur.slot], policy);
         }
-        __nanosleep(64);
+        // Scales of the stage: 16 rows x 32 groups, 4 bytes (2 groups) per
+        // cp.async.  K % 256 == 0 here, so scale rows are 4-byte aligned.
+        // Rows past the matrix are not loaded (their weights arrive
+        // zero-filled and their results are never stored).
+        const uint32_t sdst = scs + cur.slot * kStageScaleBytes;
+        const int gbase = cur.chunk * kChunkGroups;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int i = lane + 32 * k, r = i >> 4, w2 = (i & 15) * 2;
+          if (r < tr.rows && gbase + w2 < groups)
+            cp_async4(sdst + r * kScaleRowStride + w2 * 2,
+                      sscales + (size_t)(trow + r) * groups + gbase + w2);
+        }
+        cp_async_mbar_arrive(&full[cur.slot]);
+      } else {
+        const int rows = tr.rows;
+        const uint32_t bytes =
+            (uint32_t)min(kChunkGroups, groups - cur.chunk * kChunkGroups) * 64u;
+        if (lane == 0) mbar_arrive_expect_tx(&full[cur.slot], bytes * (uint32_t)rows);
+        __syncwarp();
+        if (lane < rows) {
+          const uint8_t* wbytes = reinterpret_cast<const uint8_t*>(spacked);
+          bulk_g2s(dst + lane * kPadRowStride,
+                   wbytes + (size_t)(trow + lane) * row_bytes + (size_t)cur.chunk * kRowBytes,
+                   bytes, &full[cur.slot], policy);
+        }
       }
+      cur.next(nk, stages);
     }
-    if (*abort_flag) {
+    // Stay until the copies issued last have landed: if another warp aborts,
+    // the consumers leave without waiting for them, and the CTA's shared
+    // memory must outlive every copy into it (bounded as well, against a
+    // fresh clock, and regardless of the abort flag).
+    if (lane == 0) {
+      volatile int no_abort = 0;
+      for (int s2 = max(0, issued - stages); s2 < issued; ++s2)
+        mbar_wait_bounded(&full[s2 % stages], (s2 / stages) & 1, &no_abort);
+    }
+    return;
+  }
+
+  if (warp == kConsumerWarps + 1) {
+    // ---------------- reducer: tile sums ----------------
+    // Tile t: the 16 class partials of every real row and batch column, added
+    // in class order.  It waits suspended on earlier tiles (their sums are off
+    // the critical path) and polls for the CTA's last one, whose sum and
+    // store end the kernel.
+    const int nb = min(W, p.B);
+    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
+    for (int t = 0; t < ntiles; ++t) {
+      uint64_t* bar = &red_full[t % kRedBufs];
+      const uint32_t par = (t / kRedBufs) & 1;
+      const bool ok = t + 1 < ntiles ? mbar_wait_bounded(bar, par, abort_flag)
+                                     : mbar_wait_poll_bounded(bar, par, abort_flag);
+      if (!ok) return;
+      const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
+      const TileRef tr = tiles(a, t);
+      const int trow = tr.row, rows = tr.rows;
+      if (!MULTI && t == 0 && p.out.mode == kOutKShard) {
+        pdl_wait();  // the number was advanced by the previous call's sum
+        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+      }
+      constexpr bool paired = SEG == kSegPair;
+      if (paired && tr.seg == 0) continue;  // gate tile: kept until its up tile
+      for (int o = lane; o < rows * nb; o += 32) {
+        const int r = o / nb, b = o - r * nb;
+        const float* src = rt + r * nbp + b;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kClasses; ++w) sum = __fadd_rn(sum, src[w * 16 * nbp]);
+        if constexpr (MULTI) {
+          if (paired) {
+            // h = silu(g) * u with the roundings of the unfused fp16
+            // sequence: g and u as GEMV outputs, silu(g) = g / (1 +
+            // exp(-g)) in fp32 rounded to fp16, the product in fp32
+            // rounded to fp16.
+            const float* gsrc = red + ((t - 1) % kRedBufs) * kClasses * 16 * nbp + r * nbp + b;
+            float gsum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kClasses; ++w) gsum = __fadd_rn(gsum, gsrc[w * 16 * nbp]);
+            const float gv = __half2float(__float2half_rn(gsum));
+            const float sg = __half2float(__float2half_rn(gv / (1.0f + expf(-gv))));
+            const float u = __half2float(__float2half_rn(sum));
+            const Segment& s0 = a.segs.s[0];
+            s0.y[(size_t)b * s0.rows + trow + r] = __float2half_rn(__fmul_rn(sg, u));
+          } else {
+            const Segment& sg = a.segs.s[tr.seg];
+            sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
+          }
+        } else {
+          store_y(p, b, trow + r, sum, tag);
+        }
+      }
+      __syncwarp();
       if (lane == 0) {
-        // Let copies already in flight land before the CTA's shared memory
-        // is released (bounded as well, against a fresh clock).
-        volatile int no_abort = 0;
-        for (int s = max(0, issued - stages); s < issued; ++s)
-          mbar_wait_bounded(&full[s % stages], (s / stages) & 1, &no_abort);
+        if (paired) mbar_arrive(&red_free[(t - 1) % kRedBufs]);
+        mbar_arrive(&red_free[t % kRedBufs]);
       }
-    } else {
-      signal_shards(p, lane);
     }
+    signal_shards(p, lane);
     return;
   }
 
@@ -1048,15 +1021,14 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     if (threadIdx.x == 0) mbar_arrive(xready);
   }
 
-  // Per-thread offsets, fixed for the whole kernel.
-  uint32_t offa[kGroupsPerWarp], offb[kGroupsPerWarp];
-#pragma unroll
-  for (int j = 0; j < kGroupsPerWarp; ++j) {
-    offa[j] = frag_off<TMAP>(ra, warp + j * kConsumerWarps, c);
-    offb[j] = frag_off<TMAP>(rb, warp + j * kConsumerWarps, c);
-  }
+  // Per-thread offsets, fixed for the whole kernel.  Warp w takes groups
+  // w + j * NCW (j < kGroupsPerWarp) of every stage; NCW is even, so group j's
+  // fragments sit a compile-time stride after group 0's.
+  static_assert(NCW % 2 == 0, "fragment strides assume an even warp count");
+  constexpr uint32_t kFragStride = TMAP ? (NCW / 2) * 16 * kStrip : NCW * 64;
+  const uint32_t offa = frag_off<TMAP>(ra, warp, c), offb = frag_off<TMAP>(rb, warp, c);
   const uint32_t sc_a = ra * kScaleRowStride + warp * 2, sc_b = rb * kScaleRowStride + warp * 2;
-  const uint32_t xq = xs + bb * xrow + 16 * c;  // + 256 G + 64 t
+  const uint32_t xq = xs + bb * xrow + 16 * c + 256u * warp;  // + 256 (32 chunk + NCW j) + 64 t
 
   // acc[a]: this warp's class warp + a * NCW.
   float acc[kAcc][NT][4];
@@ -1065,10 +1037,11 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
 
-  // Bulk path: scales from global memory, loaded one stage ahead.
-  float sn[kGroupsPerWarp][2];
-  auto load_scales = [&](const StageCursor& q) {
-    const TileRef tr = tiles(a, q.tile);
+  // Bulk path: scales from global memory, loaded one stage ahead (sn) and
+  // used by the stage after (scur).
+  float sn[kGroupsPerWarp][2], scur[kGroupsPerWarp][2];
+  auto load_scales = [&](int tile, int chunk) {
+    const TileRef tr = tiles(a, tile);
     const __half* sp;
     if constexpr (MULTI) {
       sp = a.segs.s[tr.seg].scales + (size_t)tr.row * groups;
@@ -1077,73 +1050,113 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
     }
 #pragma unroll
     for (int j = 0; j < kGroupsPerWarp; ++j) {
-      const int G = min(q.chunk * kChunkGroups + warp + j * kConsumerWarps, groups - 1);
+      const int G = min(chunk * kChunkGroups + warp + j * kConsumerWarps, groups - 1);
       sn[j][0] = ldg_half(sp + (size_t)min(ra, tr.rows - 1) * groups + G);
       sn[j][1] = ldg_half(sp + (size_t)min(rb, tr.rows - 1) * groups + G);
     }
   };
-  StageCursor cur;
-  if (!TMAP && total > 0) load_scales(cur);
+  if (!TMAP && total > 0) load_scales(0, 0);
 
+  // One stage.  Group j's fragments and scales are read from the slot right
+  // before its math, and the slot goes back to the producer once the warp's
+  // last group has been read; no register copy of the whole stage (the 18- or
+  // 20-warp layouts cap a thread at 96 registers: 5 warps share the busiest
+  // sub-partition's 16K).  With two n-tiles (9..16 batch rows, x from global
+  // memory) the next group's fragments are read during the current group's
+  // math instead, which measured faster there (4096^2, B = 16: 10.8 vs
+  // 11.7 us) and slower everywhere else.  FULL: all 32 groups of the chunk
+  // exist (no per-group guards).
+  struct Frag {
+    uint4 wa, wb;
+    float sa, sb;
+  };
+  auto stage = [&](auto full, uint32_t st, uint32_t sst, uint64_t* empty_bar, int chunk) {
+    constexpr bool FULL = decltype(full)::value;
+    const int cg = FULL ? kChunkGroups : groups - chunk * kChunkGroups;
+    const uint32_t xc = xq + 256u * kChunkGroups * chunk;
+    auto have = [&](int j) { return FULL || warp + j * kConsumerWarps < cg; };
+    auto load = [&](int j, Frag& f) {
+      f.wa = lds128(st + offa + j * kFragStride);
+      f.wb = lds128(st + offb + j * kFragStride);
+      if constexpr (TMAP) {
+        f.sa = lds_half(sst + sc_a + j * 2 * kConsumerWarps);
+        f.sb = lds_half(sst + sc_b + j * 2 * kConsumerWarps);
+      } else {
+        f.sa = scur[j][0];
+        f.sb = scur[j][1];
+      }
+    };
+    auto release = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar);
+    };
+    auto math = [&](int j, const Frag& f) {
+      float d[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+      if constexpr (XS) {
+        group_mma_xs(f.wa, f.wb, xc + 256u * kConsumerWarps * j, d[0]);
+      } else {
+        const int G = chunk * kChunkGroups + warp + j * kConsumerWarps;
+        group_mma_gx<NT>(f.wa, f.wb, p.x, p.ldx, p.B, G * kGroup + 32 * c, g, d);
+      }
+      scale_accumulate<NT>(acc[j % kAcc], d, f.sa, f.sb);
+    };
+    Frag f[2];
+    if constexpr (NT != 2) {
+#pragma unroll
+      for (int j = 0; j < kGroupsPerWarp; ++j) {
+        if (have(j)) load(j, f[0]);
+        if (j == kGroupsPerWarp - 1) release();
+        if (have(j)) math(j, f[0]);
+      }
+    } else {
+      if (have(0)) load(0, f[0]);
+      if (kGroupsPerWarp > 1 && have(1)) load(1, f[1]);
+      if (kGroupsPerWarp <= 2) release();
+#pragma unroll
+      for (int j = 0; j < kGroupsPerWarp; ++j) {
+        if (have(j)) math(j, f[j & 1]);
+        if (j + 2 < kGroupsPerWarp) {
+          if (have(j + 2)) load(j + 2, f[j & 1]);
+          if (j + 2 == kGroupsPerWarp - 1) release();
+        }
+      }
+    }
+  };
+
+  const bool last_chunk_full = groups % kChunkGroups == 0;
+  int slot = 0, chunk = 0, tile = 0;
+  uint32_t phase = 0;
   for (int s = 0; s < total; ++s) {
-    const int cg = min(kChunkGroups, groups - cur.chunk * kChunkGroups);
-    float sc[kGroupsPerWarp][2];
-    if (!TMAP) {
+    if (!mbar_wait_bounded(&full[slot], phase, abort_flag)) return;  // timed out: abort
+    const uint32_t st = ring + slot * kStageBytes;
+    const uint32_t sst = scs + slot * kStageScaleBytes;
+    const bool last = chunk == nk - 1;
+    if constexpr (!TMAP) {
 #pragma unroll
-      for (int j = 0; j < kGroupsPerWarp; ++j) sc[j][0] = sn[j][0], sc[j][1] = sn[j][1];
+      for (int j = 0; j < kGroupsPerWarp; ++j) scur[j][0] = sn[j][0], scur[j][1] = sn[j][1];
+      if (s + 1 < total) load_scales(last ? tile + 1 : tile, last ? 0 : chunk + 1);
     }
-    StageCursor nxt = cur;
-    nxt.next(nk, stages);
-    if (!TMAP && s + 1 < total) load_scales(nxt);
-
-    // Pull this warp's fragments (and the stage's scales) into registers and
-    // hand the slot back before computing, so the ring refills while the
-    // warps do the math.
-    uint4 wfa[kGroupsPerWarp], wfb[kGroupsPerWarp];
-    const bool have = mbar_wait_bounded(&full[cur.slot], cur.round & 1, abort_flag);
-    if (have) {
-      const uint32_t st = ring + cur.slot * kStageBytes;
-      const uint32_t sst = scs + cur.slot * kStageScaleBytes;
-#pragma unroll
-      for (int j = 0; j < kGroupsPerWarp; ++j) {
-        if (warp + j * kConsumerWarps < cg) {
-          wfa[j] = lds128(st + offa[j]);
-          wfb[j] = lds128(st + offb[j]);
-          if constexpr (TMAP) {
-            sc[j][0] = lds_half(sst + sc_a + j * 2 * kConsumerWarps);
-            sc[j][1] = lds_half(sst + sc_b + j * 2 * kConsumerWarps);
-          }
-        }
-      }
+    if (!last || last_chunk_full) {
+      stage(std::true_type{}, st, sst, &empty[slot], chunk);
+    } else {
+      stage(std::false_type{}, st, sst, &empty[slot], chunk);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[cur.slot]);
-    if (have) {
-#pragma unroll
-      for (int j = 0; j < kGroupsPerWarp; ++j) {
-        const int gi = warp + j * kConsumerWarps;
-        if (gi < cg) {
-          const int G = cur.chunk * kChunkGroups + gi;
-          float d[NT][4];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-          if constexpr (XS)
-            group_mma_xs(wfa[j], wfb[j], xq + 256u * G, d[0]);
-          else
-            group_mma_gx<NT>(wfa[j], wfb[j], p.x, p.ldx, p.B, G * kGroup + 32 * c, g, d);
-          scale_accumulate<NT>(acc[j % kAcc], d, sc[j][0], sc[j][1]);
-        }
-      }
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
     }
-
-    if (cur.chunk == nk - 1) {
+    if (last) {
       // Tile complete: each warp stores its class partials and moves on; the
       // producer warp adds them up.  A buffer is rewritten only after the
       // producer has read the tile kRedBufs back.
-      const int t = cur.tile, rs = t % kRedBufs;
+      chunk = 0;
+      const int rs = tile % kRedBufs;
       float* rt = red + rs * kClasses * 16 * nbp;
-      if (t >= kRedBufs)
-        mbar_wait_bounded(&red_free[rs], ((t / kRedBufs) - 1) & 1, abort_flag);
+      if (tile >= kRedBufs &&
+          !mbar_wait_bounded(&red_free[rs], ((tile / kRedBufs) - 1) & 1, abort_flag))
+        return;
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) {
         float* mine = rt + (warp + a * NCW) * 16 * nbp;
@@ -1155,16 +1168,15 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 8 ? 2 : 1)
             mine[rb * nbp + nt * 8 + 2 * c] = acc[a][nt][2];
             mine[rb * nbp + nt * 8 + 2 * c + 1] = acc[a][nt][3];
           }
+          acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[rs]);
-#pragma unroll
-      for (int a = 0; a < kAcc; ++a)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
+      ++tile;
+    } else {
+      ++chunk;
     }
-    cur = nxt;
   }
 }
 
@@ -1317,11 +1329,11 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
-  int units = (p.M + 7) / 8;  // one matrix: >= 8 rows per CTA
+  int units = (p.M + 15) / 16;  // one matrix: its 16-row tiles
   if constexpr (SEG != kSegOne) units = a.segs.units();
   const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), units));
   return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, dim3(grid),
-                dim3(NCW * 32 + 32), smem, st, pdl, a, p);
+                dim3(NCW * 32 + 64), smem, st, pdl, a, p);
 }
 
 // 8 consumer warps (two CTAs per SM) while a CTA's share of the weights is
@@ -1333,8 +1345,9 @@ bool use_coresident(const GemvParams& p) {
 #if defined(DK_V5_FORCE_NCW)
   return DK_V5_FORCE_NCW == 8;
 #else
-  const int grid = std::max(1, std::min(sm_count(-1), (p.M + 7) / 8));
-  const size_t cta_bytes = ((size_t)p.M + grid - 1) / grid * (size_t)p.K / 2;
+  const int tiles = (p.M + 15) / 16;
+  const int grid = std::max(1, std::min(sm_count(-1), tiles));
+  const size_t cta_bytes = (size_t)((tiles + grid - 1) / grid) * 16 * (size_t)p.K / 2;
   const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   return NT == 1 && XS && cta_bytes <= 160 * 1024 &&
          v5::layout(NT, TMAP, v5::kMinStages, xs, v5::red_cols(NT, p.B)).total <=
@@ -1731,9 +1744,11 @@ extern "C" dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate,
 // Sharded GEMV (row-parallel and K-parallel): the v5 pipeline with its
 // epilogue storing into every rank's buffer and counting the rank in.
 // ---------------------------------------------------------------------------
-// CTAs of a sharded call: one per SM, or one per 8 rows of `rows` if fewer;
-// every rank derives it from the same numbers, so every rank has the same.
-static int shard_grid(int rows) { return std::max(1, std::min(sm_count(-1), (rows + 7) / 8)); }
+// CTAs of a sharded call: one per SM, or one per 16-row tile of `rows` if
+// fewer; every rank derives it from the same numbers, so every rank has the
+// same (a rank whose shard has fewer tiles leaves some CTAs without work;
+// they still mark their arrival slots).
+static int shard_grid(int rows) { return std::max(1, std::min(sm_count(-1), (rows + 15) / 16)); }
 
 static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_gemv_config* cfg,
                               cudaStream_t st) {
