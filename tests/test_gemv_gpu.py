@@ -118,6 +118,22 @@ def test_tensor_core_family_is_bitwise_identical(cuda_device):
         assert torch.equal(y, outs[0])
 
 
+@pytest.mark.parametrize("batch", [1, 3, 8])
+def test_uneven_tile_ranges_match_the_family(batch, cuda_device):
+    # 9477 x 8192: 593 tiles over 148 CTAs, 4 or 5 each (the 16-warp streaming
+    # kernel, two 4096-k chunks per tile); the rows past M fill half of the
+    # matrix's last tile.  Bitwise the v3 kernel's outputs, and within the
+    # tolerance of the oracle.
+    M, K = 9477, 8192
+    packed, scales, x = make_problem(M, K, batch, seed=31 + batch)
+    tp, ts, tx = to_device(packed, scales, x)
+    y5 = capi_gemv(tp, ts, tx, cfg())
+    y3 = capi_gemv(tp, ts, tx, cfg(version=3))
+    assert torch.equal(y5, y3)
+    rows = (M - 300, M)
+    assert max_err(y5, oracle_y(x, packed, scales, rows=rows), rows=rows) < MAX_ABS
+
+
 def test_batch_rows_are_independent(cuda_device):
     # y[b] must not depend on which other rows share the call (bitwise), for
     # each kernel path: 1..8 rows, 9..16 rows and 17..32 rows each run on one
