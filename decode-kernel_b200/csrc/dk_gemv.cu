@@ -1317,7 +1317,7 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
 
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW, int SEG>
 dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
-                            bool pdl) {
+                            bool pdl, int ctas_per_sm = 1) {
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
@@ -1331,7 +1331,8 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
   if (s != DK_OK) return s;
   int units = (p.M + 15) / 16;  // one matrix: its 16-row tiles
   if constexpr (SEG != kSegOne) units = a.segs.units();
-  const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(sm_count(-1), units));
+  const int grid =
+      p.out.grid > 0 ? p.out.grid : std::max(1, std::min(ctas_per_sm * sm_count(-1), units));
   return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, dim3(grid),
                 dim3(NCW * 32 + 64), smem, st, pdl, a, p);
 }
@@ -1355,12 +1356,30 @@ bool use_coresident(const GemvParams& p) {
 #endif
 }
 
+// Two 8-warp CTAs of the same call per SM (grid 2 x SMs) on one large
+// matrix: each consumer warp then takes 4 groups of a stage instead of 2, so
+// the per-stage work (barrier waits, slot release, bookkeeping) is spread
+// over twice the weights.  It pays only when every CTA keeps several tiles
+// (28672x8192, B=1: 25.4 vs 26.5 us); with 1-2 tiles per CTA the SMs whose
+// CTAs differ in tile count idle half their warps (8192x28672: 33.4 vs 27.4).
+template <int NT, bool XS, bool TMAP, int SEG>
+bool use_two_ctas_per_sm(const GemvParams& p) {
+  if (!(NT == 1 && XS && TMAP && SEG == kSegOne) || p.out.grid > 0) return false;
+  const int tiles = (p.M + 15) / 16;
+  const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
+  return tiles >= 8 * sm_count(-1) &&
+         v5::layout(NT, TMAP, v5::kMinStages, xs, v5::red_cols(NT, p.B)).total <=
+             v5::smem_budget(8);
+}
+
 template <int NT, int STAMP, bool XS, bool TMAP, int SEG>
 dk_status launch_stream_w(const GemvParams& p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                           bool pdl) {
   if constexpr (NT == 1 && XS) {
     if (use_coresident<NT, XS, TMAP>(p))
       return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, SEG>(p, a, st, pdl);
+    if (use_two_ctas_per_sm<NT, XS, TMAP, SEG>(p))
+      return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, SEG>(p, a, st, pdl, 2);
   }
   return launch_stream_cfg<NT, STAMP, XS, TMAP, 16, SEG>(p, a, st, pdl);
 }
