@@ -69,7 +69,9 @@ struct OutSpec {
   unsigned* slots[kMaxShards] = {};  // shard modes: each rank's arrival slots
   unsigned* seq = nullptr;           // shard modes: this rank's [calls done, grid]
   int grid = 0;                      // shard modes: CTAs per rank (same on every rank)
-  int await_all = 0;                 // CTA 0 waits for every rank's part
+  int await_all = 0;                 // row shards: CTA 0 waits for every rank's part;
+                                     // K shards: the kernel sums the world's partials
+                                     // of its rows into fp16 y (GemvParams::y)
 };
 
 // v5 row segments: several weight matrices sharing x, run as one GEMV over
@@ -225,6 +227,58 @@ __device__ __forceinline__ void signal_shards(const GemvParams& p, int lane) {
     if (lane == 0) p.out.seq[0] = epoch;
   }
   if (lane == 0) p.out.seq[1] = gridDim.x;
+}
+
+// K-shard mode with the sum fused (ranks on separate GPUs, running at once):
+// after this CTA has stored its partials of all its tiles into every rank's
+// buffer, it polls this rank's buffer for every rank's word of the same rows
+// -- the same CTA of every rank owns the same rows -- until each carries this
+// call's number, adds the ranks in order (0 + p_0 + p_1 + ..., the
+// arithmetic of dk_shard_reduce, so the same bits) and stores fp16 y.  The
+// CTA that finishes last advances the call number (seq[0]; seq[2] counts the
+// CTAs), as the separate sum's last block does.  Bounded: 2 s after the first
+// poll it records kDevWaitTimeout and stops.  Called by the tile-sum warp,
+// all lanes.
+template <class Args, class Tiles>
+__device__ __forceinline__ void sum_kshards(const GemvParams& p, const Args& a, const Tiles& tiles,
+                                            int ntiles, int nb, unsigned tag, int lane,
+                                            volatile int* abort_flag) {
+  const unsigned long long* part =
+      static_cast<const unsigned long long*>(p.out.dst[p.out.rank]);
+  const size_t rank_stride = (size_t)p.B * p.M;
+  const uint64_t t0 = globaltimer_ns();
+  bool timed_out = false;
+  for (int t = 0; t < ntiles && !timed_out; ++t) {
+    const TileRef tr = tiles(a, t);
+    for (int o = lane; o < tr.rows * nb; o += 32) {
+      const int r = o / nb, b = o - r * nb;
+      const size_t i = (size_t)b * p.M + tr.row + r;
+      float sum = 0.f;
+      for (int g = 0; g < p.out.world; ++g) {
+        unsigned long long w = ld_ll_sys(part + g * rank_stride + i);
+        for (unsigned polls = 1; (unsigned)(w >> 32) != tag; ++polls) {
+          if ((polls & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
+            if (!*abort_flag) atomicExch(&g_dk_device_error, kDevWaitTimeout);
+            *abort_flag = 1;
+            timed_out = true;
+            break;
+          }
+          w = ld_ll_sys(part + g * rank_stride + i);
+        }
+        sum = __fadd_rn(sum, __uint_as_float((unsigned)w));
+      }
+      p.y[i] = __float2half_rn(sum);
+    }
+    timed_out = __any_sync(0xffffffffu, timed_out);
+  }
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(p.out.seq + 2, 1u) == gridDim.x - 1) {
+      p.out.seq[2] = 0;
+      p.out.seq[0] = tag;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -938,7 +992,11 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     // the critical path) and polls for the CTA's last one, whose sum and
     // store end the kernel.
     const int nb = min(W, p.B);
-    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
+    unsigned tag = 0;  // K-shard mode: this call's sequence number
+    if (!MULTI && p.out.mode == kOutKShard) {
+      pdl_wait();  // the number was advanced by the previous call's sum
+      tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+    }
     for (int t = 0; t < ntiles; ++t) {
       uint64_t* bar = &red_full[t % kRedBufs];
       const uint32_t par = (t / kRedBufs) & 1;
@@ -948,10 +1006,6 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
       const TileRef tr = tiles(a, t);
       const int trow = tr.row, rows = tr.rows;
-      if (!MULTI && t == 0 && p.out.mode == kOutKShard) {
-        pdl_wait();  // the number was advanced by the previous call's sum
-        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
-      }
       constexpr bool paired = SEG == kSegPair;
       if (paired && tr.seg == 0) continue;  // gate tile: kept until its up tile
       for (int o = lane; o < rows * nb; o += 32) {
@@ -989,6 +1043,8 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
         mbar_arrive(&red_free[t % kRedBufs]);
       }
     }
+    if (!MULTI && p.out.mode == kOutKShard && p.out.await_all) sum_kshards(p, a, tiles, ntiles, nb,
+                                                                           tag, lane, abort_flag);
     signal_shards(p, lane);
     return;
   }
@@ -1770,7 +1826,7 @@ extern "C" dk_status dk_w4a16_gemv_silu_mul(const int32_t* packed_gate,
 static int shard_grid(int rows) { return std::max(1, std::min(sm_count(-1), (rows + 15) / 16)); }
 
 static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_gemv_config* cfg,
-                              cudaStream_t st) {
+                              cudaStream_t st, bool fused_sum = false) {
   stamp_begin_call();
   dk_gemv_config c;
   dk_gemv_config_init(&c);
@@ -1779,7 +1835,7 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   if (s != DK_OK) return s;
   if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
   const bool kshard = p.out.mode == kOutKShard;
-  const bool await_all = (c.flags & DK_FLAG_SHARD_WAIT) != 0 && !kshard;
+  const bool await_all = kshard ? fused_sum : (c.flags & DK_FLAG_SHARD_WAIT) != 0;
   if (sm_count(-1) > DK_SHARD_SLOTS) return DK_ERR_UNSUPPORTED;
   if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
       !g->seq)
@@ -1803,7 +1859,7 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   p.out.await_all = await_all ? 1 : 0;
   p.ws = nullptr;
   p.counters = nullptr;
-  p.y = nullptr;
+  if (!fused_sum) p.y = nullptr;
   const bool pdl = (c.flags & DK_FLAG_PDL) != 0;
   return c.reuse_weights ? launch_stream_nt<kStampReuse>(p, st, pdl)
                          : launch_stream_nt<5>(p, st, pdl);
@@ -1848,6 +1904,28 @@ extern "C" dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t*
   p.out.ld = M;
   p.out.grid = shard_grid(M);
   return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" dk_status dk_w4a16_gemv_kshard_sum(const int32_t* packed, const uint16_t* scales,
+                                              const uint16_t* x, int ldx, int M, int K_shard,
+                                              int B, const dk_shard_group* group, uint16_t* y,
+                                              const dk_gemv_config* cfg, void* stream) {
+  stamp_begin_call();
+  if (!y || (reinterpret_cast<uintptr_t>(y) & 1u)) return DK_ERR_INVALID_ARG;
+  if (group && group->world >= 1 && (!group->seq)) return DK_ERR_INVALID_ARG;
+  GemvParams p;
+  p.packed = reinterpret_cast<const uint32_t*>(packed);
+  p.scales = reinterpret_cast<const __half*>(scales);
+  p.x = reinterpret_cast<const __half*>(x);
+  p.y = reinterpret_cast<__half*>(y);
+  p.M = M;
+  p.K = K_shard;
+  p.ldx = ldx;
+  p.B = B;
+  p.out.mode = kOutKShard;
+  p.out.ld = M;
+  p.out.grid = shard_grid(M);
+  return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream), true);
 }
 
 // ---------------------------------------------------------------------------

@@ -375,15 +375,30 @@ class KParallelW4A16:
         which = self.peers.begin()
         groups = {r: self.peers.group(r, which) for r in self.shards}
         for r, (p, s, k0) in self.shards.items():
-            _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), x.data_ptr() + 2 * k0,
-                                            self.K, self.M, p.shape[1] * 8, B,
-                                            ctypes.byref(groups[r]), ctypes.byref(cfg), st),
-                   "dk_w4a16_gemv_kshard")
+            self._kshard(lib, p, s, x.data_ptr() + 2 * k0, self.K, B, groups[r], cfg, st, r,
+                         inline)
+        if not inline:
+            self._reduce(lib, groups, B, st)
+        return self.out[r0][:B]
+
+    def _kshard(self, lib, p, s, x_ptr, ldx, B, group, cfg, st, r, inline):
+        """Ranks on their own GPUs: the GEMV sums the world's partials itself
+        (dk_w4a16_gemv_kshard_sum); emulated ranks sharing one GPU store their
+        partials and are summed afterwards (dk_shard_reduce)."""
+        if inline:
+            _check(lib.dk_w4a16_gemv_kshard_sum(p.data_ptr(), s.data_ptr(), x_ptr, ldx, self.M,
+                                                p.shape[1] * 8, B, ctypes.byref(group),
+                                                self.out[r][:B].data_ptr(), ctypes.byref(cfg),
+                                                st), "dk_w4a16_gemv_kshard_sum")
+        else:
+            _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), x_ptr, ldx, self.M,
+                                            p.shape[1] * 8, B, ctypes.byref(group),
+                                            ctypes.byref(cfg), st), "dk_w4a16_gemv_kshard")
+
+    def _reduce(self, lib, groups, B, st):
         for r in self.shards:
             _check(lib.dk_shard_reduce(ctypes.byref(groups[r]), self.M, B,
-                                       self.out[r][:B].data_ptr(), int(inline), st),
-                   "dk_shard_reduce")
-        return self.out[r0][:B]
+                                       self.out[r][:B].data_ptr(), 0, st), "dk_shard_reduce")
 
     def forward_local(self, xs: dict, pdl: bool = False) -> torch.Tensor:
         """Like ``__call__``, but each local rank r brings only its own K
@@ -420,13 +435,9 @@ class KParallelW4A16:
         groups = {r: self.peers.group(r, which) for r in self.shards}
         for r, (p, s, _) in self.shards.items():
             kn = p.shape[1] * 8
-            _check(lib.dk_w4a16_gemv_kshard(p.data_ptr(), s.data_ptr(), xs[r].data_ptr(), kn,
-                                            self.M, kn, B, ctypes.byref(groups[r]),
-                                            ctypes.byref(cfg), st), "dk_w4a16_gemv_kshard")
-        for r in self.shards:
-            _check(lib.dk_shard_reduce(ctypes.byref(groups[r]), self.M, B,
-                                       self.out[r][:B].data_ptr(), int(inline), st),
-                   "dk_shard_reduce")
+            self._kshard(lib, p, s, xs[r].data_ptr(), kn, B, groups[r], cfg, st, r, inline)
+        if not inline:
+            self._reduce(lib, groups, B, st)
         return self.out[r0][:B]
 
     def _nccl_local(self, xs: torch.Tensor) -> torch.Tensor:

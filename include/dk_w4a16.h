@@ -129,7 +129,7 @@ DK_API dk_status dk_w4a16_gemv(const int32_t* packed, const uint16_t* scales, co
  *    passes of up to 8 rows, so the need is the arrival counters
  *    (ceil(M/16) * 4 bytes, rounded up to 256) plus M * (K/128) * min(B, 8)
  *    * 4 bytes: about M * K <= 268M weights at B = 1, and M * K <= 33M
- *    weights at B >= 8 (4096 x 8176 fits, 4096 x 8192 does not).  A split
+ *    weights at B >= 8 (M x K = 8176 x 4096 fits, 8192 x 4096 does not).  A split
  *    that clamps to 1 (K = 128) needs no scratch at all.
  *  - The first call on a device looks up the buffer's device address with that
  *    device current; make that first call before any stream capture.  The
@@ -241,6 +241,20 @@ DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* sca
                                       const uint16_t* x, int ldx, int M, int K_shard, int B,
                                       const dk_shard_group* group, const dk_gemv_config* cfg,
                                       void* stream);
+
+/* K-parallel shard with the sum fused in: as dk_w4a16_gemv_kshard, and then
+ * the same kernel adds the world's partials of its rows -- in rank order, the
+ * bits of dk_shard_reduce -- into this rank's fp16 y [B, M] and advances
+ * seq[0], so no dk_shard_reduce follows (and a PDL-launched successor already
+ * streams its weights during the exchange).  Every CTA polls the peers' words
+ * for its own rows, so the ranks' calls must run at the same time on
+ * different GPUs: ranks that share a GPU use dk_w4a16_gemv_kshard and
+ * dk_shard_reduce.  Bounded like dk_shard_reduce.  No counterpart in the
+ * reference (single-GPU). */
+DK_API dk_status dk_w4a16_gemv_kshard_sum(const int32_t* packed, const uint16_t* scales,
+                                          const uint16_t* x, int ldx, int M, int K_shard, int B,
+                                          const dk_shard_group* group, uint16_t* y,
+                                          const dk_gemv_config* cfg, void* stream);
 
 /* Enqueue the wait for the sharded call just made on this group: until every
  * arrival slot of this rank's array carries seq[0] + 1, then seq[0] += 1.
