@@ -992,11 +992,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     // the critical path) and polls for the CTA's last one, whose sum and
     // store end the kernel.
     const int nb = min(W, p.B);
-    unsigned tag = 0;  // K-shard mode: this call's sequence number
-    if (!MULTI && p.out.mode == kOutKShard) {
-      pdl_wait();  // the number was advanced by the previous call's sum
-      tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
-    }
+    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
     for (int t = 0; t < ntiles; ++t) {
       uint64_t* bar = &red_full[t % kRedBufs];
       const uint32_t par = (t / kRedBufs) & 1;
@@ -1006,6 +1002,10 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
       const TileRef tr = tiles(a, t);
       const int trow = tr.row, rows = tr.rows;
+      if (!MULTI && t == 0 && p.out.mode == kOutKShard) {
+        pdl_wait();  // the number was advanced by the previous call's sum
+        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+      }
       constexpr bool paired = SEG == kSegPair;
       if (paired && tr.seg == 0) continue;  // gate tile: kept until its up tile
       for (int o = lane; o < rows * nb; o += 32) {
@@ -1043,8 +1043,17 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
         mbar_arrive(&red_free[t % kRedBufs]);
       }
     }
-    if (!MULTI && p.out.mode == kOutKShard && p.out.await_all) sum_kshards(p, a, tiles, ntiles, nb,
-                                                                           tag, lane, abort_flag);
+    // (one n-tile only: the code would cost the 2- and 4-n-tile kernels registers;
+    // larger batches take the separate sum, dk_w4a16_gemv_kshard_sum)
+    if constexpr (!MULTI && NT == 1) {
+      if (p.out.mode == kOutKShard && p.out.await_all) {
+        if (ntiles == 0) {  // a CTA without rows still counts itself in
+          pdl_wait();
+          tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+        }
+        sum_kshards(p, a, tiles, ntiles, nb, tag, lane, abort_flag);
+      }
+    }
     signal_shards(p, lane);
     return;
   }
@@ -1925,7 +1934,11 @@ extern "C" dk_status dk_w4a16_gemv_kshard_sum(const int32_t* packed, const uint1
   p.out.mode = kOutKShard;
   p.out.ld = M;
   p.out.grid = shard_grid(M);
-  return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream), true);
+  if (B <= 8) return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream), true);
+  // 9..32 rows: the GEMV stores its partials, a separate kernel sums them (the same bits)
+  const dk_status s = shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
+  if (s != DK_OK) return s;
+  return dk_shard_reduce(group, M, B, y, 1, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -249,8 +249,10 @@ DK_API dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t* sca
  * streams its weights during the exchange).  Every CTA polls the peers' words
  * for its own rows, so the ranks' calls must run at the same time on
  * different GPUs: ranks that share a GPU use dk_w4a16_gemv_kshard and
- * dk_shard_reduce.  Bounded like dk_shard_reduce.  No counterpart in the
- * reference (single-GPU). */
+ * dk_shard_reduce.  Up to 8 batch rows the sum runs inside the GEMV; with 9..32
+ * this call enqueues the GEMV and then dk_shard_reduce (two launches, the same
+ * bits).  Bounded like dk_shard_reduce.  No counterpart in the reference
+ * (single-GPU). */
 DK_API dk_status dk_w4a16_gemv_kshard_sum(const int32_t* packed, const uint16_t* scales,
                                           const uint16_t* x, int ldx, int M, int K_shard, int B,
                                           const dk_shard_group* group, uint16_t* y,

@@ -272,13 +272,19 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         tp = torch.from_numpy(packed).to(dev)
         ts = torch.from_numpy(scales.view(np.int16)).to(dev).view(torch.float16)
         tx = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.float16)
-        peers = PeerBuffers(8 * world * B * max(M, K))
+        peers = PeerBuffers(8 * world * 12 * max(M, K))
         rowl = RowParallelW4A16(tp, ts, peers, max_batch=B)
         kl = KParallelW4A16(tp, ts, peers, max_batch=B)
         y_row = rowl(tx).clone()
         y_k = kl(tx).clone()
         y_row_nccl = RowParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
         y_k_nccl = KParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
+        # 12 batch rows: above the 8 that the GEMV sums in-kernel, so the
+        # K-parallel call stores partials and a separate kernel sums them.
+        x12 = torch.from_numpy(make_problem(M, K, 12, seed=79)[2].view(np.int16)).to(dev)
+        x12 = x12.view(torch.float16)
+        y_k12 = KParallelW4A16(tp, ts, peers, max_batch=12)(x12).clone()
+        y_k12_nccl = KParallelW4A16(tp, ts, peers, max_batch=12, exchange="nccl")(x12)
         # Tensor-parallel MLP (gate/up = W, down = W's first K rows as [K, M]
         # shapes): real ranks, NCCL, and both ranks emulated on this GPU.
         from decode_kernel.sharded import TensorParallelMLP
@@ -299,6 +305,7 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         np.savez(f"{out_path}.{rank}.npz", row=y_row.float().cpu().numpy(),
                  k=y_k.float().cpu().numpy(), row_nccl=y_row_nccl.float().cpu().numpy(),
                  k_nccl=y_k_nccl.float().cpu().numpy(), tp=y_tp.float().cpu().numpy(),
+                 k12=y_k12.float().cpu().numpy(), k12_nccl=y_k12_nccl.float().cpu().numpy(),
                  tp_nccl=y_tp_nccl.float().cpu().numpy(), tp_emu=y_tp_emu.float().cpu().numpy(),
                  err=err)
         dist.barrier()
@@ -332,5 +339,6 @@ def test_two_real_ranks_fused_and_nccl(tmp_path):
         # real ranks equal the emulated ones bit for bit
         assert np.array_equal(g["tp"], g["tp_emu"]) and np.array_equal(g["tp"], g["tp_nccl"])
         assert np.array_equal(g["tp"], got[0]["tp"])
+        assert np.array_equal(g["k12"], g["k12_nccl"]) and np.array_equal(g["k12"], got[0]["k12"])
         for key in ("row", "k", "row_nccl", "k_nccl"):
             assert np.abs(g[key] - ref).max() < MAX_ABS, key
