@@ -1429,7 +1429,8 @@ bool use_coresident(const GemvParams& p) {
 // CTAs differ in tile count idle half their warps (8192x28672: 33.4 vs 27.4).
 template <int NT, bool XS, bool TMAP, int SEG>
 bool use_two_ctas_per_sm(const GemvParams& p) {
-  if (!(NT == 1 && XS && TMAP && SEG == kSegOne) || p.out.grid > 0) return false;
+  if (!(NT == 1 && XS && TMAP && (SEG == kSegOne || SEG == kSegPair)) || p.out.grid > 0)
+    return false;
   const int tiles = (p.M + 15) / 16;
   const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   return tiles >= 8 * sm_count(-1) &&
