@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(vb::kThreads, 1)
         if (lane < p.B) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < rows) store_y(p, lane, r0 + c0 + j, acc[j]);
+            if (c0 + j < rows) store_y<false>(p, lane, r0 + c0 + j, acc[j]);
         }
       }
       tcgen05_fence_before();

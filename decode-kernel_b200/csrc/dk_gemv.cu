@@ -59,6 +59,10 @@ enum OutMode : int {
   kOutRowShard = 2,  // fp16 into every rank's dst[g] [B, ld] at columns col0 + m
   kOutKShard = 3,    // fp32 partial into every rank's dst[g] [world][B][M], slot `rank`, as
                      // 64-bit {value, call number} words (low-latency exchange)
+  kOutRowGather = 4, // row shard, low-latency exchange: every rank's dst[g] [B, ld] of 64-bit
+                     // {fp16-rounded value as fp32, call number} words at columns col0 + m
+                     // (the K-shard words' format); the kernel then gathers the whole
+                     // [B, ld] of fp16 into y (GemvParams::y)
 };
 constexpr int kMaxShards = DK_MAX_SHARDS;
 struct OutSpec {
@@ -183,6 +187,9 @@ struct CtaTiles {
 
 // v5 result store for batch row b, output row m.  `tag`: the call's sequence
 // number (K-shard mode only).
+// GATHER: the kernel compiles the row-gather words (one n-tile kernels only: the
+// code costs the 2- and 4-n-tile kernels registers they do not have).
+template <bool GATHER>
 __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float v,
                                         unsigned tag = 0) {
   switch (p.out.mode) {
@@ -200,6 +207,15 @@ __device__ __forceinline__ void store_y(const GemvParams& p, int b, int m, float
         st_ll_sys(static_cast<unsigned long long*>(p.out.dst[g]) +
                       ((size_t)p.out.rank * p.B + b) * p.M + m,
                   v, tag);
+      break;
+    case kOutRowGather:
+      if constexpr (GATHER) {
+        const float h = __half2float(__float2half_rn(v));  // fp16 -> fp32 -> fp16 is exact
+        for (int g = 0; g < p.out.world; ++g)
+          st_ll_sys(static_cast<unsigned long long*>(p.out.dst[g]) + (size_t)b * p.out.ld +
+                        p.out.col0 + m,
+                    h, tag);
+      }
       break;
     default:
       p.y[(size_t)b * p.M + m] = __float2half_rn(v);
@@ -268,6 +284,55 @@ __device__ __forceinline__ void sum_kshards(const GemvParams& p, const Args& a, 
         sum = __fadd_rn(sum, __uint_as_float((unsigned)w));
       }
       p.y[i] = __float2half_rn(sum);
+    }
+    timed_out = __any_sync(0xffffffffu, timed_out);
+  }
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(p.out.seq + 2, 1u) == gridDim.x - 1) {
+      p.out.seq[2] = 0;
+      p.out.seq[0] = tag;
+    }
+  }
+}
+
+// Row shards with the gather fused (ranks on separate GPUs, running at once):
+// after this CTA has stored its rows into every rank's buffer as 64-bit
+// {value, call number} words, it takes its share [bid·ld/grid, (bid+1)·ld/grid)
+// of the full gathered width, polls this rank's buffer until each of those
+// words carries this call's number (whichever rank wrote it), and stores the
+// fp16 values into y [B, ld].  The words carry their own call number -- the
+// full 32 bits, so no stale word of another layer's exchange in the same
+// buffer set can pass for this call's -- and neither a fence behind the stores
+// nor an arrival handshake is needed.  The CTA that finishes last advances the
+// call number (seq[0]; seq[2] counts the CTAs).  Bounded like sum_kshards.
+// Called by the tile-sum warp, all lanes.
+__device__ __forceinline__ void gather_rows(const GemvParams& p, unsigned tag, int lane,
+                                            volatile int* abort_flag) {
+  const unsigned long long* words = static_cast<const unsigned long long*>(p.out.dst[p.out.rank]);
+  const int ld = p.out.ld;
+  const int g0 = (int)((long long)blockIdx.x * ld / gridDim.x);
+  const int g1 = (int)((long long)(blockIdx.x + 1) * ld / gridDim.x);
+  const int n = g1 - g0;
+  const uint64_t t0 = globaltimer_ns();
+  bool timed_out = false;
+  for (int o0 = 0; o0 < n * p.B && !timed_out; o0 += 32) {
+    const int o = o0 + lane;
+    if (o < n * p.B) {
+      const int b = o / n, m = g0 + (o - b * n);
+      const size_t i = (size_t)b * ld + m;
+      unsigned long long w = ld_ll_sys(words + i);
+      for (unsigned polls = 1; (unsigned)(w >> 32) != tag; ++polls) {
+        if ((polls & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
+          if (!*abort_flag) atomicExch(&g_dk_device_error, kDevWaitTimeout);
+          *abort_flag = 1;
+          timed_out = true;
+          break;
+        }
+        w = ld_ll_sys(words + i);
+      }
+      p.y[i] = __float2half_rn(__uint_as_float((unsigned)w));
     }
     timed_out = __any_sync(0xffffffffu, timed_out);
   }
@@ -1002,7 +1067,8 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
       const TileRef tr = tiles(a, t);
       const int trow = tr.row, rows = tr.rows;
-      if (!MULTI && t == 0 && p.out.mode == kOutKShard) {
+      if (!MULTI && t == 0 &&
+          (p.out.mode == kOutKShard || (NT == 1 && p.out.mode == kOutRowGather))) {
         pdl_wait();  // the number was advanced by the previous call's sum
         tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
       }
@@ -1034,7 +1100,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
             sg.y[(size_t)b * sg.rows + trow + r] = __float2half_rn(sum);
           }
         } else {
-          store_y(p, b, trow + r, sum, tag);
+          store_y<!MULTI && NT == 1>(p, b, trow + r, sum, tag);
         }
       }
       __syncwarp();
@@ -1046,13 +1112,14 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     // (one n-tile only: the code would cost the 2- and 4-n-tile kernels registers;
     // larger batches take the separate sum, dk_w4a16_gemv_kshard_sum)
     if constexpr (!MULTI && NT == 1) {
-      if (p.out.mode == kOutKShard && p.out.await_all) {
-        if (ntiles == 0) {  // a CTA without rows still counts itself in
-          pdl_wait();
-          tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
-        }
-        sum_kshards(p, a, tiles, ntiles, nb, tag, lane, abort_flag);
+      const bool ksum = p.out.mode == kOutKShard && p.out.await_all;
+      const bool gather = p.out.mode == kOutRowGather;
+      if ((ksum || gather) && ntiles == 0) {  // a CTA without rows still counts itself in
+        pdl_wait();
+        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
       }
+      if (ksum) sum_kshards(p, a, tiles, ntiles, nb, tag, lane, abort_flag);
+      if (gather) gather_rows(p, tag, lane, abort_flag);
     }
     signal_shards(p, lane);
     return;
@@ -1845,13 +1912,15 @@ static dk_status shard_launch(GemvParams p, const dk_shard_group* g, const dk_ge
   if (s != DK_OK) return s;
   if (c.version != 5 || (c.flags & DK_FLAG_F32_OUT)) return DK_ERR_UNSUPPORTED;
   const bool kshard = p.out.mode == kOutKShard;
-  const bool await_all = kshard ? fused_sum : (c.flags & DK_FLAG_SHARD_WAIT) != 0;
+  const bool gather = p.out.mode == kOutRowGather;
+  const bool await_all =
+      kshard ? fused_sum : !gather && (c.flags & DK_FLAG_SHARD_WAIT) != 0;
   if (sm_count(-1) > DK_SHARD_SLOTS) return DK_ERR_UNSUPPORTED;
   if (!g || g->world < 1 || g->world > kMaxShards || g->rank < 0 || g->rank >= g->world ||
       !g->seq)
     return DK_ERR_INVALID_ARG;
   for (int i = 0; i < g->world; ++i)
-    if (!g->bufs[i] || (!kshard && !g->slots[i]) ||
+    if (!g->bufs[i] || (!kshard && !gather && !g->slots[i]) ||
         (kshard && (reinterpret_cast<uintptr_t>(g->bufs[i]) & 7u)))
       return DK_ERR_INVALID_ARG;
   if (p.M <= 0 || p.K <= 0 || p.K % DK_GROUP_SIZE != 0 || p.B <= 0) return DK_ERR_INVALID_ARG;
@@ -1914,6 +1983,35 @@ extern "C" dk_status dk_w4a16_gemv_kshard(const int32_t* packed, const uint16_t*
   p.out.ld = M;
   p.out.grid = shard_grid(M);
   return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" dk_status dk_w4a16_gemv_rowshard_gather(const int32_t* packed, const uint16_t* scales,
+                                                   const uint16_t* x, int M_shard, int row0,
+                                                   int M_total, int K, int B,
+                                                   const dk_shard_group* group, uint16_t* y,
+                                                   const dk_gemv_config* cfg, void* stream) {
+  stamp_begin_call();
+  if (M_shard <= 0 || row0 < 0 || M_total < row0 + M_shard) return DK_ERR_INVALID_ARG;
+  if (!y || (reinterpret_cast<uintptr_t>(y) & 1u)) return DK_ERR_INVALID_ARG;
+  if (B > 8) return DK_ERR_UNSUPPORTED;  // one n-tile only (the row-shard call serves more)
+  if (group)
+    for (int i = 0; i < group->world && i < DK_MAX_SHARDS; ++i)
+      if (reinterpret_cast<uintptr_t>(group->bufs[i]) & 7u) return DK_ERR_INVALID_ARG;
+  GemvParams p;
+  p.packed = reinterpret_cast<const uint32_t*>(packed);
+  p.scales = reinterpret_cast<const __half*>(scales);
+  p.x = reinterpret_cast<const __half*>(x);
+  p.y = reinterpret_cast<__half*>(y);
+  p.M = M_shard;
+  p.K = K;
+  p.ldx = K;
+  p.B = B;
+  p.out.mode = kOutRowGather;
+  p.out.ld = M_total;
+  p.out.col0 = row0;
+  if (group && group->world >= 1)  // the same on every rank: from the largest shard
+    p.out.grid = shard_grid((M_total + group->world - 1) / group->world);
+  return shard_launch(p, group, cfg, static_cast<cudaStream_t>(stream), true);
 }
 
 extern "C" dk_status dk_w4a16_gemv_kshard_sum(const int32_t* packed, const uint16_t* scales,

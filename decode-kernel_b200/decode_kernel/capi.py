@@ -73,6 +73,9 @@ SIGNATURES = {
     "dk_w4a16_gemv_kshard": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
                                   ctypes.POINTER(GemvConfig), _P]),
     "dk_shard_wait": (_I, [ctypes.POINTER(ShardGroup), _P]),
+    "dk_w4a16_gemv_rowshard_gather": (_I, [_P, _P, _P, _I, _I, _I, _I, _I,
+                                           ctypes.POINTER(ShardGroup), _P,
+                                           ctypes.POINTER(GemvConfig), _P]),
     "dk_w4a16_gemv_kshard_sum": (_I, [_P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(ShardGroup),
                                       _P, ctypes.POINTER(GemvConfig), _P]),
     "dk_shard_reduce": (_I, [ctypes.POINTER(ShardGroup), _I, _I, _P, _I, _P]),

@@ -266,7 +266,11 @@ class RowParallelW4A16:
 
     ``packed``/``scales`` are the FULL tensors; each local rank keeps its rows
     on the current GPU.  Call with the replicated x; returns the gathered
-    fp16 y on every rank (a view of a buffer the call after next reuses).
+    fp16 y on every rank.  Ranks on their own GPUs with up to 8 batch rows
+    exchange {value, call number} words and the GEMV gathers them into this
+    layer's own output (valid until its next call); otherwise the rows are
+    stored as fp16 into the peer buffers, marked by arrival slots, and y is a
+    view of a buffer the call after next reuses.
     """
 
     def __init__(self, packed: torch.Tensor, scales: torch.Tensor, peers: PeerBuffers,
@@ -276,14 +280,15 @@ class RowParallelW4A16:
         self.M, self.K = packed.shape[0], packed.shape[1] * 8
         self.peers, self.exchange, self.group = peers, exchange, group
         self.max_batch = int(max_batch)
-        if 2 * self.max_batch * self.M > peers.nbytes:
-            raise ValueError("peer buffers too small for [max_batch, M] fp16")
+        if 8 * self.max_batch * self.M > peers.nbytes:
+            raise ValueError("peer buffers too small for [max_batch, M] 64-bit words")
         dev = self.dev = torch.device("cuda", torch.cuda.current_device())
         self.shards = {}
         for r in peers.local_ranks():
             p, s, row0 = slice_rows(packed, scales, peers.world, r)
             # own copies, so the caller's full tensors can be freed
             self.shards[r] = (p.to(dev).clone(), s.to(dev).clone(), row0)
+        self.out = torch.empty((self.max_batch, self.M), dtype=torch.float16, device=dev)
 
     def __call__(self, x: torch.Tensor, pdl: bool = False) -> torch.Tensor:
         x = _as_batch(x, self.K, self.max_batch, self.dev)
@@ -302,6 +307,16 @@ class RowParallelW4A16:
         # Ranks on their own GPUs wait inside the kernel; emulated ranks
         # sharing this GPU's stream wait after all of them have run.
         inline = not self.peers.emulated
+        if inline and B <= 8:
+            group = self.peers.group(r0, which)
+            p, s, row0 = self.shards[r0]
+            _check(lib.dk_w4a16_gemv_rowshard_gather(p.data_ptr(), s.data_ptr(), x.data_ptr(),
+                                                     p.shape[0], row0, self.M, self.K, B,
+                                                     ctypes.byref(group),
+                                                     self.out[:B].data_ptr(),
+                                                     ctypes.byref(_cfg(pdl)), st),
+                   "dk_w4a16_gemv_rowshard_gather")
+            return self.out[:B]
         cfg = _cfg(pdl, await_all=inline)
         groups = {r: self.peers.group(r, which) for r in self.shards}
         for r, (p, s, row0) in self.shards.items():

@@ -229,6 +229,24 @@ DK_API dk_status dk_w4a16_gemv_rowshard(const int32_t* packed, const uint16_t* s
                                         int K, int B, const dk_shard_group* group,
                                         const dk_gemv_config* cfg, void* stream);
 
+/* Row-parallel shard with the gather fused in, for ranks on separate GPUs
+ * running at once, B <= 8 (DK_ERR_UNSUPPORTED above).  As
+ * dk_w4a16_gemv_rowshard, but every output travels as one 64-bit word
+ * {the fp16-rounded value as fp32 in the low half, the call's sequence number
+ * seq[0] + 1 in the high half} -- the K-parallel words' format -- into every
+ * rank's bufs[g] (8-byte aligned, [B, M_total] words, columns row0 ..
+ * row0 + M_shard - 1), and the same kernel then gathers the whole width:
+ * each CTA polls its share of this rank's words until they carry this call's
+ * number and writes them to y, fp16 [B, M_total], and the last CTA advances
+ * seq[0].  No release fence, slot array or separate wait (slots may be NULL);
+ * the two-set rule above applies.  Bounded like dk_shard_wait.  No
+ * counterpart in the reference (single-GPU). */
+DK_API dk_status dk_w4a16_gemv_rowshard_gather(const int32_t* packed, const uint16_t* scales,
+                                               const uint16_t* x, int M_shard, int row0,
+                                               int M_total, int K, int B,
+                                               const dk_shard_group* group, uint16_t* y,
+                                               const dk_gemv_config* cfg, void* stream);
+
 /* K-parallel shard: this rank holds a group-aligned K slice of an [M, K]
  * weight as its own contiguous packed [M, K_shard/8] and scales
  * [M, K_shard/128]; x points at the slice's first column of the full fp16 x,

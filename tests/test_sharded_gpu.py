@@ -62,7 +62,7 @@ def test_row_parallel_emulated_is_the_unsharded_gemv(world, B, cuda_device):
     M, K = 1376, 4096
     packed, scales, x = make_problem(M, K, B, seed=200 + world)
     tp, ts, tx = to_device(packed, scales, x)
-    peers = PeerBuffers(2 * B * M, emulate=world)
+    peers = PeerBuffers(8 * B * M, emulate=world)
     layer = RowParallelW4A16(tp, ts, peers, max_batch=B)
     try:
         for call in range(3):  # both buffer sets, counters accumulating
@@ -156,7 +156,7 @@ def test_row_parallel_step_replays_from_a_cuda_graph(cuda_device):
     M, K, B, world = 1024, 2048, 1, 4
     packed, scales, x = make_problem(M, K, B, seed=5)
     tp, ts, tx = to_device(packed, scales, x)
-    peers = PeerBuffers(2 * B * M, emulate=world)
+    peers = PeerBuffers(8 * B * M, emulate=world)
     layer = RowParallelW4A16(tp, ts, peers, max_batch=B)
     try:
         xin = tx.clone()
@@ -275,8 +275,9 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         peers = PeerBuffers(8 * world * 12 * max(M, K))
         rowl = RowParallelW4A16(tp, ts, peers, max_batch=B)
         kl = KParallelW4A16(tp, ts, peers, max_batch=B)
-        y_row = rowl(tx).clone()
-        y_k = kl(tx).clone()
+        for _ in range(3):  # both buffer sets, the call number advancing
+            y_row = rowl(tx).clone()
+            y_k = kl(tx).clone()
         y_row_nccl = RowParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
         y_k_nccl = KParallelW4A16(tp, ts, peers, max_batch=B, exchange="nccl")(tx)
         # 12 batch rows: above the 8 that the GEMV sums in-kernel, so the
@@ -285,6 +286,10 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
         x12 = x12.view(torch.float16)
         y_k12 = KParallelW4A16(tp, ts, peers, max_batch=12)(x12).clone()
         y_k12_nccl = KParallelW4A16(tp, ts, peers, max_batch=12, exchange="nccl")(x12)
+        # ... and the gathered row-parallel call with 12 rows takes the
+        # fp16 stores with arrival slots instead of the in-kernel gather.
+        y_row12 = RowParallelW4A16(tp, ts, peers, max_batch=12)(x12).clone()
+        y_row12_nccl = RowParallelW4A16(tp, ts, peers, max_batch=12, exchange="nccl")(x12)
         # Tensor-parallel MLP (gate/up = W, down = W's first K rows as [K, M]
         # shapes): real ranks, NCCL, and both ranks emulated on this GPU.
         from decode_kernel.sharded import TensorParallelMLP
@@ -306,6 +311,8 @@ def _rank_main(rank: int, world: int, port: int, out_path: str) -> None:
                  k=y_k.float().cpu().numpy(), row_nccl=y_row_nccl.float().cpu().numpy(),
                  k_nccl=y_k_nccl.float().cpu().numpy(), tp=y_tp.float().cpu().numpy(),
                  k12=y_k12.float().cpu().numpy(), k12_nccl=y_k12_nccl.float().cpu().numpy(),
+                 row12=y_row12.float().cpu().numpy(),
+                 row12_nccl=y_row12_nccl.float().cpu().numpy(),
                  tp_nccl=y_tp_nccl.float().cpu().numpy(), tp_emu=y_tp_emu.float().cpu().numpy(),
                  err=err)
         dist.barrier()
@@ -340,5 +347,6 @@ def test_two_real_ranks_fused_and_nccl(tmp_path):
         assert np.array_equal(g["tp"], g["tp_emu"]) and np.array_equal(g["tp"], g["tp_nccl"])
         assert np.array_equal(g["tp"], got[0]["tp"])
         assert np.array_equal(g["k12"], g["k12_nccl"]) and np.array_equal(g["k12"], got[0]["k12"])
+        assert np.array_equal(g["row12"], g["row12_nccl"])
         for key in ("row", "k", "row_nccl", "k_nccl"):
             assert np.abs(g[key] - ref).max() < MAX_ABS, key
