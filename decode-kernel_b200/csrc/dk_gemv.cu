@@ -289,7 +289,6 @@ __device__ __forceinline__ void sum_kshards(const GemvParams& p, const Args& a, 
   }
   __syncwarp();
   if (lane == 0) {
-    __threadfence();
     if (atomicAdd(p.out.seq + 2, 1u) == gridDim.x - 1) {
       p.out.seq[2] = 0;
       p.out.seq[0] = tag;
@@ -338,7 +337,6 @@ __device__ __forceinline__ void gather_rows(const GemvParams& p, unsigned tag, i
   }
   __syncwarp();
   if (lane == 0) {
-    __threadfence();
     if (atomicAdd(p.out.seq + 2, 1u) == gridDim.x - 1) {
       p.out.seq[2] = 0;
       p.out.seq[0] = tag;
@@ -1057,7 +1055,17 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     // the critical path) and polls for the CTA's last one, whose sum and
     // store end the kernel.
     const int nb = min(W, p.B);
-    unsigned tag = 0;  // K-shard mode: this call's sequence number, read before the first sum
+    // Word-exchange modes: this call's number (the previous call advanced
+    // it).  One n-tile reads it while the consumers stage x, off the path
+    // from the first tile's partials to its stores; the wider kernels read it
+    // at their first tile (earlier costs them registers).
+    unsigned tag = 0;
+    if constexpr (!MULTI && NT == 1) {
+      if (p.out.mode == kOutKShard || p.out.mode == kOutRowGather) {
+        pdl_wait();
+        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
+      }
+    }
     for (int t = 0; t < ntiles; ++t) {
       uint64_t* bar = &red_full[t % kRedBufs];
       const uint32_t par = (t / kRedBufs) & 1;
@@ -1067,8 +1075,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
       const TileRef tr = tiles(a, t);
       const int trow = tr.row, rows = tr.rows;
-      if (!MULTI && t == 0 &&
-          (p.out.mode == kOutKShard || (NT == 1 && p.out.mode == kOutRowGather))) {
+      if (!MULTI && NT != 1 && t == 0 && p.out.mode == kOutKShard) {
         pdl_wait();  // the number was advanced by the previous call's sum
         tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
       }
@@ -1114,10 +1121,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     if constexpr (!MULTI && NT == 1) {
       const bool ksum = p.out.mode == kOutKShard && p.out.await_all;
       const bool gather = p.out.mode == kOutRowGather;
-      if ((ksum || gather) && ntiles == 0) {  // a CTA without rows still counts itself in
-        pdl_wait();
-        tag = *reinterpret_cast<volatile const unsigned*>(p.out.seq) + 1;
-      }
+      // (a CTA without rows takes part too: it counts itself in)
       if (ksum) sum_kshards(p, a, tiles, ntiles, nb, tag, lane, abort_flag);
       if (gather) gather_rows(p, tag, lane, abort_flag);
     }
@@ -1472,7 +1476,13 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
 // 8 consumer warps (two CTAs per SM) while a CTA's share of the weights is
 // small -- then a CTA's life is dominated by latency and overlapping the next
 // GEMV pays most -- and while the 8-warp layout keeps at least 2 stages in
-// half of the SM's shared memory; 16 warps otherwise.
+// half of the SM's shared memory; 16 warps otherwise.  A 16-warp CTA shares
+// its SM with no other CTA (registers), so a GEMV next to one in a stream
+// gets no overlap on either side: in the Llama-2-7B layer sequence the
+// 4096x11008 down projection (176 KB per CTA) on 8 warps takes the 32-layer
+// step from 1621 to 1263 us although alone it is 4 % slower (8.46 vs 8.15
+// us).  Shares above 192 KB stay on 16 warps: with 8 warps the Llama-3-8B
+// MLP (224-229 KB) made that model's step slower (1483 -> 1839 us).
 template <int NT, bool XS, bool TMAP>
 bool use_coresident(const GemvParams& p) {
 #if defined(DK_V5_FORCE_NCW)
@@ -1482,7 +1492,7 @@ bool use_coresident(const GemvParams& p) {
   const int grid = std::max(1, std::min(sm_count(-1), tiles));
   const size_t cta_bytes = (size_t)((tiles + grid - 1) / grid) * 16 * (size_t)p.K / 2;
   const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
-  return NT == 1 && XS && cta_bytes <= 160 * 1024 &&
+  return NT == 1 && XS && cta_bytes <= 192 * 1024 &&
          v5::layout(NT, TMAP, v5::kMinStages, xs, v5::red_cols(NT, p.B)).total <=
              v5::smem_budget(8);
 #endif
