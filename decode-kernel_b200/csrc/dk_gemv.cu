@@ -1451,6 +1451,47 @@ bool weight_tensor_map(const void* packed, int M, int K, CUtensorMap* out) {
   return true;
 }
 
+// Per (device, stream): whether the last k_stream launch there ran exactly
+// one 8-warp CTA on every SM.  Only then does each SM keep one CTA slot free
+// for a PDL-launched successor, so that the successor's CTAs land one per SM;
+// after a 16-warp kernel, two CTAs of the same call per SM or a grid smaller
+// than the SM count, the SMs that free first can take two of them and finish
+// last.  A hint for the next launch's warp count only: a stale or wrong entry
+// costs time, never results (every warp count computes the same bits).
+class StreamHistory {
+ public:
+  bool one_per_sm(int device, cudaStream_t st) {
+    std::lock_guard<std::mutex> lk(mu_);
+    for (const Entry& e : e_)
+      if (e.stamp && e.device == device && e.st == st) return e.one_per_sm;
+    return false;
+  }
+  void record(int device, cudaStream_t st, bool one_per_sm) {
+    std::lock_guard<std::mutex> lk(mu_);
+    Entry* victim = &e_[0];
+    for (Entry& e : e_) {
+      if (e.stamp && e.device == device && e.st == st) {
+        victim = &e;
+        break;
+      }
+      if (e.stamp < victim->stamp) victim = &e;
+    }
+    *victim = Entry{st, device, one_per_sm, ++clock_};
+  }
+
+ private:
+  struct Entry {
+    cudaStream_t st;
+    int device;
+    bool one_per_sm;
+    unsigned long long stamp;
+  };
+  std::mutex mu_;
+  Entry e_[32] = {};
+  unsigned long long clock_ = 0;
+};
+StreamHistory g_stream_history;
+
 template <int NT, int STAMP, bool XS, bool TMAP, int NCW, int SEG>
 dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                             bool pdl, int ctas_per_sm = 1) {
@@ -1467,10 +1508,12 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
   if (s != DK_OK) return s;
   int units = (p.M + 15) / 16;  // one matrix: its 16-row tiles
   if constexpr (SEG != kSegOne) units = a.segs.units();
-  const int grid =
-      p.out.grid > 0 ? p.out.grid : std::max(1, std::min(ctas_per_sm * sm_count(-1), units));
-  return launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, dim3(grid),
-                dim3(NCW * 32 + 64), smem, st, pdl, a, p);
+  const int sms = sm_count(-1);
+  const int grid = p.out.grid > 0 ? p.out.grid : std::max(1, std::min(ctas_per_sm * sms, units));
+  s = launch("k_stream", k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, dim3(grid),
+             dim3(NCW * 32 + 64), smem, st, pdl, a, p);
+  if (s == DK_OK) g_stream_history.record(current_device(), st, NCW == 8 && grid == sms);
+  return s;
 }
 
 // 8 consumer warps (two CTAs per SM) while a CTA's share of the weights is
@@ -1481,10 +1524,15 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
 // gets no overlap on either side: in the Llama-2-7B layer sequence the
 // 4096x11008 down projection (176 KB per CTA) on 8 warps takes the 32-layer
 // step from 1621 to 1263 us although alone it is 4 % slower (8.46 vs 8.15
-// us).  Shares above 192 KB stay on 16 warps: with 8 warps the Llama-3-8B
-// MLP (224-229 KB) made that model's step slower (1483 -> 1839 us).
+// us) -- but only behind a launch that left one slot free on every SM
+// (StreamHistory): behind the SiLU-mul pair (two CTAs per SM) the same
+// projection in the tensor-parallel layer sequence is faster on 16 warps
+// (1137 vs 1245 us per 32 layers), and so is the 12288-row q/k/v launch
+// (192 KB) behind it (1245 vs 1331).  Shares above 192 KB stay on 16 warps:
+// with 8 warps the Llama-3-8B MLP (224-229 KB) made that model's step slower
+// (1483 -> 1839 us).
 template <int NT, bool XS, bool TMAP>
-bool use_coresident(const GemvParams& p) {
+bool use_coresident(const GemvParams& p, cudaStream_t st) {
 #if defined(DK_V5_FORCE_NCW)
   return DK_V5_FORCE_NCW == 8;
 #else
@@ -1492,7 +1540,10 @@ bool use_coresident(const GemvParams& p) {
   const int grid = std::max(1, std::min(sm_count(-1), tiles));
   const size_t cta_bytes = (size_t)((tiles + grid - 1) / grid) * 16 * (size_t)p.K / 2;
   const int xs = XS ? p.B * v5::xs_row_stride(p.K) : 0;
-  return NT == 1 && XS && cta_bytes <= 192 * 1024 &&
+  const size_t limit =
+      (cta_bytes > 160 * 1024 && g_stream_history.one_per_sm(current_device(), st) ? 192 : 160) *
+      1024;
+  return NT == 1 && XS && cta_bytes <= limit &&
          v5::layout(NT, TMAP, v5::kMinStages, xs, v5::red_cols(NT, p.B)).total <=
              v5::smem_budget(8);
 #endif
@@ -1519,7 +1570,7 @@ template <int NT, int STAMP, bool XS, bool TMAP, int SEG>
 dk_status launch_stream_w(const GemvParams& p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                           bool pdl) {
   if constexpr (NT == 1 && XS) {
-    if (use_coresident<NT, XS, TMAP>(p))
+    if (use_coresident<NT, XS, TMAP>(p, st))
       return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, SEG>(p, a, st, pdl);
     if (use_two_ctas_per_sm<NT, XS, TMAP, SEG>(p))
       return launch_stream_cfg<NT, STAMP, XS, TMAP, 8, SEG>(p, a, st, pdl, 2);
