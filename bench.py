@@ -1113,11 +1113,16 @@ def run_ours(args) -> None:
 def model_gemvs(workload: str, layers: int):
     """(M, K, layout) of every GEMV in one decode step of the model shapes:
     Llama-2-7B (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008; all
-    row-parallel -- 86 groups of K in down do not divide by 4 or 8) and
+    row-parallel -- 86 groups of K in down do not divide by 4 or 8),
+    Llama-3-8B (q/o 4096x4096, k/v 1024x4096 -- 8 kv heads of 128 --,
+    gate/up 14336x4096 row-parallel, down 4096x14336 K-parallel) and
     Llama-70B-shaped layers (q/o 8192x8192 and gate/up 28672x8192
     row-parallel, down 8192x28672 K-parallel)."""
     if workload == "llama7b":
         one = [(4096, 4096, "row")] * 4 + [(11008, 4096, "row")] * 2 + [(4096, 11008, "row")]
+    elif workload == "llama8b":
+        one = ([(4096, 4096, "row"), (1024, 4096, "row"), (1024, 4096, "row"), (4096, 4096, "row")]
+               + [(14336, 4096, "row")] * 2 + [(4096, 14336, "k")])
     else:
         one = [(8192, 8192, "row"), (8192, 8192, "row"), (28672, 8192, "row"),
                (28672, 8192, "row"), (8192, 28672, "k")]
@@ -1142,7 +1147,7 @@ def run_sharded(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     B = args.batch
-    layers = args.layers or (32 if args.workload == "llama7b" else 8)
+    layers = args.layers or (32 if args.workload in ("llama7b", "llama8b") else 8)
     shapes = model_gemvs(args.workload, layers)
     maxm = max(m for m, _, _ in shapes)
     peers = PeerBuffers(max(2 * B * maxm, 8 * ws * B * maxm))
@@ -1296,9 +1301,10 @@ def main() -> None:
     ap.add_argument("--no-isolated", action="store_true",
                     help="skip the isolated-call timing under the reference's protocol")
     ap.add_argument("--workload",
-                    choices=["gemv", "llama7b", "llama70b", "llama7b-tp", "llama70b-tp"],
+                    choices=["gemv", "llama7b", "llama8b", "llama70b", "llama7b-tp",
+                             "llama70b-tp"],
                     default="gemv",
-                    help="gemv: the BASELINE metric; llama7b / llama70b: the sharded model "
+                    help="gemv: the BASELINE metric; llama7b / llama8b / llama70b: the sharded model "
                          "decode-step GEMV stacks, every GEMV gathered (strong scaling over "
                          "the ranks); llama7b-tp / llama70b-tp: the same layers in the "
                          "tensor-parallel layout, two exchanges per layer")

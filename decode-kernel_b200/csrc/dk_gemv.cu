@@ -262,28 +262,47 @@ __device__ __forceinline__ void sum_kshards(const GemvParams& p, const Args& a, 
   const unsigned long long* part =
       static_cast<const unsigned long long*>(p.out.dst[p.out.rank]);
   const size_t rank_stride = (size_t)p.B * p.M;
+  const int world = p.out.world;
+  // One pass over all of this CTA's (row, batch column) outputs, 32 at a
+  // time.  Each lane first loads every rank's word of its output -- the
+  // loads are independent, so they are in flight together -- and then polls
+  // again only the words that do not carry this call's number yet: the wait
+  // costs about one L2 round trip per pass, not one per rank and tile.
+  const int per_tile = 16 * nb;
+  const int total = ntiles * per_tile;
   const uint64_t t0 = globaltimer_ns();
   bool timed_out = false;
-  for (int t = 0; t < ntiles && !timed_out; ++t) {
-    const TileRef tr = tiles(a, t);
-    for (int o = lane; o < tr.rows * nb; o += 32) {
-      const int r = o / nb, b = o - r * nb;
-      const size_t i = (size_t)b * p.M + tr.row + r;
+  for (int o0 = 0; o0 < total && !timed_out; o0 += 32) {
+    const int o = o0 + lane;
+    const int t = o / per_tile, q = o - t * per_tile, r = q / nb, b = q - r * nb;
+    bool live = o < total;
+    size_t i = 0;
+    if (live) {
+      const TileRef tr = tiles(a, t);
+      live = r < tr.rows;
+      i = (size_t)b * p.M + tr.row + r;
+    }
+    if (live) {
+      unsigned long long w[kMaxShards];
+#pragma unroll
+      for (int g = 0; g < kMaxShards; ++g)
+        if (g < world) w[g] = ld_ll_sys(part + g * rank_stride + i);
       float sum = 0.f;
-      for (int g = 0; g < p.out.world; ++g) {
-        unsigned long long w = ld_ll_sys(part + g * rank_stride + i);
-        for (unsigned polls = 1; (unsigned)(w >> 32) != tag; ++polls) {
+#pragma unroll
+      for (int g = 0; g < kMaxShards; ++g) {
+        if (g >= world) break;
+        for (unsigned polls = 1; (unsigned)(w[g] >> 32) != tag && !timed_out; ++polls) {
           if ((polls & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
             if (!*abort_flag) atomicExch(&g_dk_device_error, kDevWaitTimeout);
             *abort_flag = 1;
             timed_out = true;
-            break;
+          } else {
+            w[g] = ld_ll_sys(part + g * rank_stride + i);
           }
-          w = ld_ll_sys(part + g * rank_stride + i);
         }
-        sum = __fadd_rn(sum, __uint_as_float((unsigned)w));
+        sum = __fadd_rn(sum, __uint_as_float((unsigned)w[g]));
       }
-      p.y[i] = __float2half_rn(sum);
+      if (!timed_out) p.y[i] = __float2half_rn(sum);
     }
     timed_out = __any_sync(0xffffffffu, timed_out);
   }
@@ -314,24 +333,37 @@ __device__ __forceinline__ void gather_rows(const GemvParams& p, unsigned tag, i
   const int g0 = (int)((long long)blockIdx.x * ld / gridDim.x);
   const int g1 = (int)((long long)(blockIdx.x + 1) * ld / gridDim.x);
   const int n = g1 - g0;
+  // kU words per lane per pass: loaded together, then polled again only
+  // where they do not carry this call's number yet.
+  constexpr int kU = 4;
   const uint64_t t0 = globaltimer_ns();
   bool timed_out = false;
-  for (int o0 = 0; o0 < n * p.B && !timed_out; o0 += 32) {
-    const int o = o0 + lane;
-    if (o < n * p.B) {
-      const int b = o / n, m = g0 + (o - b * n);
-      const size_t i = (size_t)b * ld + m;
-      unsigned long long w = ld_ll_sys(words + i);
-      for (unsigned polls = 1; (unsigned)(w >> 32) != tag; ++polls) {
+  for (int o0 = 0; o0 < n * p.B && !timed_out; o0 += 32 * kU) {
+    unsigned long long w[kU];
+    long long idx[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int o = o0 + u * 32 + lane;
+      idx[u] = -1;
+      if (o < n * p.B) {
+        const int b = o / n, m = g0 + (o - b * n);
+        idx[u] = (long long)b * ld + m;
+        w[u] = ld_ll_sys(words + idx[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (idx[u] < 0) continue;
+      for (unsigned polls = 1; (unsigned)(w[u] >> 32) != tag && !timed_out; ++polls) {
         if ((polls & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
           if (!*abort_flag) atomicExch(&g_dk_device_error, kDevWaitTimeout);
           *abort_flag = 1;
           timed_out = true;
-          break;
+        } else {
+          w[u] = ld_ll_sys(words + idx[u]);
         }
-        w = ld_ll_sys(words + i);
       }
-      p.y[i] = __float2half_rn(__uint_as_float((unsigned)w));
+      if (!timed_out) p.y[idx[u]] = __float2half_rn(__uint_as_float((unsigned)w[u]));
     }
     timed_out = __any_sync(0xffffffffu, timed_out);
   }
