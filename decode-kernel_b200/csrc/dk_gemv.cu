@@ -114,6 +114,7 @@ struct GemvParams {
   unsigned* counters;      // v4: one arrival counter per 16-row tile
   int stages;              // v5: ring depth
   int xs_bytes;            // v5: bytes of x staged in shared memory (0 = none)
+  int red_bufs;            // v5: tile-sum buffers (2 or 4)
   OutSpec out;             // v5: destination of y
 };
 
@@ -840,10 +841,12 @@ struct Layout {
 // so a consumer warp reaching the end of a tile never waits for the producer
 // to have added up the tile before last.  One n-tile keeps only the batch
 // columns that exist (rounded up to the even pair a quad lane stores).
-constexpr int kRedBufs = 4;
+constexpr int kRedBufs = 4;     // at most; GemvParams::red_bufs is the launch's count
+constexpr int kMinRedBufs = 2;  // (a launch uses 2 or 4: the ring index is a mask)
 __host__ __device__ inline int red_cols(int nt, int B) { return nt == 1 ? ((B + 1) & ~1) : 8 * nt; }
 
-__host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_bytes, int nbp) {
+__host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_bytes, int nbp,
+                                         int red_bufs = kRedBufs) {
   Layout L;
   int off = stages * stage_bytes(tmap);
   L.sc_off = off;
@@ -851,7 +854,7 @@ __host__ __device__ inline Layout layout(int nt, bool tmap, int stages, int xs_b
   L.xs_off = off;
   off += (xs_bytes + 127) / 128 * 128;
   L.red_off = off;
-  off += kRedBufs * kClasses * 16 * nbp * (int)sizeof(float);
+  off += red_bufs * kClasses * 16 * nbp * (int)sizeof(float);
   L.bar_off = off;
   off += (2 * kMaxStages + 2 * kRedBufs + 1) * 8 + 16;  // full, empty, red_full, red_free, xready, flag
   L.total = off;
@@ -954,7 +957,11 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
   constexpr int W = 8 * NT;  // mma output columns per tile row
   const int stages = p.stages;
   const int nbp = red_cols(NT, p.B);
-  const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0, nbp);
+  // Tile-sum buffers in use, 2 or 4: ring slot t & (n - 1), round t >> (n / 2).
+  // Only the 16-warp kernel ever runs with 2 (the largest staged x); the
+  // 8-warp kernels keep the count a constant.
+  const int nred = NCW == 8 ? kRedBufs : p.red_bufs, rmask = nred - 1, rshift = nred >> 1;
+  const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0, nbp, nred);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + kMaxStages;
   uint64_t* red_full = empty + kMaxStages;    // [kRedBufs]: all consumer warps stored a tile
@@ -1099,12 +1106,12 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       }
     }
     for (int t = 0; t < ntiles; ++t) {
-      uint64_t* bar = &red_full[t % kRedBufs];
-      const uint32_t par = (t / kRedBufs) & 1;
+      uint64_t* bar = &red_full[t & rmask];
+      const uint32_t par = (t >> rshift) & 1;
       const bool ok = t + 1 < ntiles ? mbar_wait_bounded(bar, par, abort_flag)
                                      : mbar_wait_poll_bounded(bar, par, abort_flag);
       if (!ok) return;
-      const float* rt = red + (t % kRedBufs) * kClasses * 16 * nbp;
+      const float* rt = red + (t & rmask) * kClasses * 16 * nbp;
       const TileRef tr = tiles(a, t);
       const int trow = tr.row, rows = tr.rows;
       if (!MULTI && NT != 1 && t == 0 && p.out.mode == kOutKShard) {
@@ -1125,7 +1132,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
             // sequence: g and u as GEMV outputs, silu(g) = g / (1 +
             // exp(-g)) in fp32 rounded to fp16, the product in fp32
             // rounded to fp16.
-            const float* gsrc = red + ((t - 1) % kRedBufs) * kClasses * 16 * nbp + r * nbp + b;
+            const float* gsrc = red + ((t - 1) & rmask) * kClasses * 16 * nbp + r * nbp + b;
             float gsum = 0.f;
 #pragma unroll
             for (int w = 0; w < kClasses; ++w) gsum = __fadd_rn(gsum, gsrc[w * 16 * nbp]);
@@ -1144,8 +1151,8 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
       }
       __syncwarp();
       if (lane == 0) {
-        if (paired) mbar_arrive(&red_free[(t - 1) % kRedBufs]);
-        mbar_arrive(&red_free[t % kRedBufs]);
+        if (paired) mbar_arrive(&red_free[(t - 1) & rmask]);
+        mbar_arrive(&red_free[t & rmask]);
       }
     }
     // (one n-tile only: the code would cost the 2- and 4-n-tile kernels registers;
@@ -1173,16 +1180,50 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     // as pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7), at chunk 4t + c of its
     // group.  Loads go through L2 only (x may have just been written by the
     // predecessor grid; no L1 line from an earlier kernel is trusted).
+    // The thread's chunks j = tid, tid + T, ... of the flattened [B, K/8]
+    // array are loaded kXLoads at a time before any of them is stored: the
+    // shared store is a compiler barrier, so a load-store loop would wait one
+    // L2 round trip per chunk, and the issuer holds the weight stream back
+    // until x has landed.
+    constexpr int kXLoads = 8;
     const int cpr = p.K / 8;
-    for (int b = 0; b < p.B; ++b) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)b * p.ldx);
-      const uint32_t rowbase = xs + (uint32_t)(b * xrow);
-#pragma unroll 4
-      for (int i = threadIdx.x; i < cpr; i += kConsumerThreads) {
-        uint32_t pr[4];
-        pair_x8(ldcg128(src + i), pr);
-        const int ii = i & 15;
-        sts128(rowbase + (uint32_t)(i >> 4) * 256u + 16u * (4 * (ii & 3) + (ii >> 2)), pr);
+    if (p.B * cpr <= 2 * kConsumerThreads) {
+      for (int b = 0; b < p.B; ++b) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)b * p.ldx);
+        const uint32_t rowbase = xs + (uint32_t)(b * xrow);
+#pragma unroll 2
+        for (int i = threadIdx.x; i < cpr; i += kConsumerThreads) {
+          uint32_t pr[4];
+          pair_x8(ldcg128(src + i), pr);
+          const int ii = i & 15;
+          sts128(rowbase + (uint32_t)(i >> 4) * 256u + 16u * (4 * (ii & 3) + (ii >> 2)), pr);
+        }
+      }
+    } else {
+      int b = 0, i = threadIdx.x;
+      while (i >= cpr) i -= cpr, ++b;
+      while (b < p.B) {
+        uint4 v[kXLoads];
+        uint32_t dst[kXLoads];
+#pragma unroll
+        for (int u = 0; u < kXLoads; ++u) {
+          dst[u] = 0xffffffffu;
+          if (b < p.B) {
+            v[u] = ldcg128(reinterpret_cast<const uint4*>(p.x + (size_t)b * p.ldx) + i);
+            const int ii = i & 15;
+            dst[u] = xs + (uint32_t)(b * xrow) + (uint32_t)(i >> 4) * 256u +
+                     16u * (4 * (ii & 3) + (ii >> 2));
+            for (i += kConsumerThreads; i >= cpr; i -= cpr) ++b;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kXLoads; ++u) {
+          if (dst[u] != 0xffffffffu) {
+            uint32_t pr[4];
+            pair_x8(v[u], pr);
+            sts128(dst[u], pr);
+          }
+        }
       }
     }
     named_barrier(1, kConsumerThreads);
@@ -1318,12 +1359,12 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
     if (last) {
       // Tile complete: each warp stores its class partials and moves on; the
       // producer warp adds them up.  A buffer is rewritten only after the
-      // producer has read the tile kRedBufs back.
+      // producer has read the tile red_bufs back.
       chunk = 0;
-      const int rs = tile % kRedBufs;
+      const int rs = tile & rmask;
       float* rt = red + rs * kClasses * 16 * nbp;
-      if (tile >= kRedBufs &&
-          !mbar_wait_bounded(&red_free[rs], ((tile / kRedBufs) - 1) & 1, abort_flag))
+      if (tile >= nred &&
+          !mbar_wait_bounded(&red_free[rs], ((tile >> rshift) - 1) & 1, abort_flag))
         return;
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) {
@@ -1530,11 +1571,14 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
   static std::atomic<unsigned long long> smem_done{0};
   p.xs_bytes = XS ? p.B * v5::xs_row_stride(p.K) : 0;
   p.stages = v5::kMaxStages;
-  while (p.stages > v5::kMinStages &&
-         v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total >
-             v5::smem_budget(NCW))
-    --p.stages;
-  const size_t smem = v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B)).total;
+  p.red_bufs = v5::kRedBufs;
+  auto total = [&]() {
+    return v5::layout(NT, TMAP, p.stages, p.xs_bytes, v5::red_cols(NT, p.B), p.red_bufs).total;
+  };
+  // Ring depth first, then (only for the largest staged x) tile-sum buffers.
+  while (p.stages > v5::kMinStages && total() > v5::smem_budget(NCW)) --p.stages;
+  if (NCW == 16 && total() > v5::smem_budget(NCW)) p.red_bufs = v5::kMinRedBufs;
+  const size_t smem = total();
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, v5::kSmemCap, smem_done);
   if (s != DK_OK) return s;
@@ -1615,8 +1659,9 @@ dk_status launch_stream_w(const GemvParams& p, const StreamArgs<SEG != kSegOne>&
 template <int NT, int STAMP, bool TMAP, int SEG>
 dk_status launch_stream_x(const GemvParams& p, const StreamArgs<SEG != kSegOne>& a, cudaStream_t st,
                           bool pdl) {
-  if (NT == 1 && (size_t)p.B * v5::xs_row_stride(p.K) <= (size_t)v5::kXsMaxBytes)
-    return launch_stream_w<1, STAMP, true, TMAP, SEG>(p, a, st, pdl);
+  const int xs = p.B * v5::xs_row_stride(p.K);
+  const bool staged = xs <= v5::kXsMaxBytes || v5::layout(1, TMAP, v5::kMinStages, xs, v5::red_cols(1, p.B), v5::kMinRedBufs).total <= v5::smem_budget(16);
+  if (NT == 1 && staged) return launch_stream_w<1, STAMP, true, TMAP, SEG>(p, a, st, pdl);
   return launch_stream_w<NT, STAMP, false, TMAP, SEG>(p, a, st, pdl);
 }
 

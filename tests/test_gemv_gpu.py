@@ -234,6 +234,49 @@ def test_baseline_shapes(shape, batch, cuda_device):
         assert max_err(capi_gemv(tp, ts, tx, c), ref) < MAX_ABS
 
 
+# x rows above 68 KB staged in shared memory by the 16-warp streaming kernel:
+# the ring shrinks to 2-3 stages and, for the largest x (K = 8192, B = 8;
+# K = 11008, B = 6), the tile sums run on 2 buffers instead of 4.  Ragged M
+# (partial last tiles), bitwise against the register-tiled v3 kernel (same
+# canonical order) and within the tolerance of the oracle.
+LARGE_X = [(300, 8192, 5), (1000, 8192, 8), (4109, 8192, 6), (257, 11008, 4), (999, 11008, 6),
+           (64, 28672, 2)]
+
+
+@pytest.mark.parametrize("M,K,B", LARGE_X)
+def test_large_staged_x_bitwise_v3_and_oracle(M, K, B, cuda_device):
+    packed, scales, x = make_problem(M, K, B, seed=4000 + M + B, std=0.05)
+    tp, ts, tx = to_device(packed, scales, x)
+    y5 = capi_gemv(tp, ts, tx, cfg())
+    assert stamp() == 5
+    assert torch.equal(y5, capi_gemv(tp, ts, tx, cfg(version=3)))
+    assert max_err(y5, oracle_y(x, packed, scales)) < MAX_ABS
+    from decode_kernel import capi
+
+    assert capi.load().dk_device_error(-1, 0) == 0
+
+
+@pytest.mark.parametrize("M,K,B", [(1000, 8192, 8), (2050, 8192, 6)])
+def test_large_staged_x_pair_and_multi(M, K, B, cuda_device):
+    # The gate/up pair (its gate tile is held until the up tile's sum, so on
+    # 2 tile-sum buffers both are in use) and a two-matrix launch, against
+    # single-matrix v3 GEMVs.
+    import torch.nn.functional as F
+
+    from decode_kernel import capi, gemv_multi, gemv_silu_mul
+
+    pg, sg, x = make_problem(M, K, B, seed=4100 + M + B, std=0.05)
+    pu, su, _ = make_problem(M + 37, K, 1, seed=4200 + M + B, std=0.05)
+    tg, tsg, tx = to_device(pg, sg, x)
+    tu, tsu, _ = to_device(pu, su, x)
+    g3, u3 = capi_gemv(tg, tsg, tx, cfg(version=3)), capi_gemv(tu, tsu, tx, cfg(version=3))
+    ys = gemv_multi([(tg, tsg), (tu, tsu)], tx)
+    assert torch.equal(ys[0], g3) and torch.equal(ys[1], u3)
+    h = gemv_silu_mul((tg, tsg), (tu[:M], tsu[:M]), tx)
+    assert torch.equal(h, F.silu(g3) * u3[:, :M])
+    assert capi.load().dk_device_error(-1, 0) == 0
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("shape", [(28672, 8192), (8192, 28672), (8192, 8192)])
 @pytest.mark.parametrize("batch", [1, 8])
