@@ -784,7 +784,9 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_tile(GemvParams p) {
 // halves of the banks, so every fragment load is conflict-free.  (The padded
 // bulk layout is conflict-free with the identity mapping.)
 //
-// Activations: when the pass's x rows fit in kXsMaxBytes the consumers load
+// Activations: when the pass's x rows fit in kXsMaxBytes -- or, on the 16-warp
+// kernel, in what is left beside a 2-stage ring and 2 tile-sum buffers (x up to
+// ~130 KB: K = 8192 at 8 rows) -- the consumers load
 // them once (after the PDL wait -- x may be the previous kernel's output) and
 // store every 128-k group rearranged so that a group's B fragments are four
 // conflict-free 128-bit loads: the pairs of word t for quad lane c sit at
@@ -958,9 +960,11 @@ __global__ void __launch_bounds__(NCW * 32 + 64, NCW == 8 ? 2 : 1)
   const int stages = p.stages;
   const int nbp = red_cols(NT, p.B);
   // Tile-sum buffers in use, 2 or 4: ring slot t & (n - 1), round t >> (n / 2).
-  // Only the 16-warp kernel ever runs with 2 (the largest staged x); the
-  // 8-warp kernels keep the count a constant.
-  const int nred = NCW == 8 ? kRedBufs : p.red_bufs, rmask = nred - 1, rshift = nred >> 1;
+  // Only the 16-warp one-n-tile kernel with x staged ever runs with 2 (the
+  // largest staged x); every other kernel keeps the count a constant (a
+  // runtime count costs the 2- and 4-n-tile kernels spills).
+  constexpr bool kRuntimeRed = NCW == 16 && NT == 1 && XS;
+  const int nred = kRuntimeRed ? p.red_bufs : kRedBufs, rmask = nred - 1, rshift = nred >> 1;
   const Layout L = layout(NT, TMAP, stages, XS ? p.xs_bytes : 0, nbp, nred);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + kMaxStages;
@@ -1577,7 +1581,7 @@ dk_status launch_stream_cfg(GemvParams p, const StreamArgs<SEG != kSegOne>& a, c
   };
   // Ring depth first, then (only for the largest staged x) tile-sum buffers.
   while (p.stages > v5::kMinStages && total() > v5::smem_budget(NCW)) --p.stages;
-  if (NCW == 16 && total() > v5::smem_budget(NCW)) p.red_bufs = v5::kMinRedBufs;
+  if (NCW == 16 && NT == 1 && XS && total() > v5::smem_budget(NCW)) p.red_bufs = v5::kMinRedBufs;
   const size_t smem = total();
   if (smem > (size_t)v5::kSmemCap) return DK_ERR_UNSUPPORTED;
   dk_status s = ensure_smem(k_stream<NT, STAMP, XS, TMAP, NCW, SEG>, v5::kSmemCap, smem_done);
