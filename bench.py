@@ -636,6 +636,82 @@ SWEEP_SHAPES = [(11008, 4096, 1), (4096, 11008, 1), (28672, 8192, 1), (8192, 286
 SWEEP_BATCHES = [1, 2, 4, 8, 16, 32]
 
 
+# The reference's cross-precision reference points (bench/bench.py:106-155 of
+# the reference): an fp16 weight matrix through cuBLAS -- torch.mv at B = 1
+# (a GEMV), torch.mm above -- and through F.linear.  Not a peer (4x the weight
+# bytes): it shows where a dense fp16 GEMV sits on this GPU.
+FP16_SHAPES = [(4096, 4096, 1), (4096, 4096, 8), (4096, 4096, 32), (11008, 4096, 1),
+               (4096, 11008, 1)]
+
+
+def fp16_bytes(m: int, k: int, b: int) -> int:
+    """Bytes an fp16 GEMV moves: W + x + y (bench/common.py:120-121 of the
+    reference)."""
+    return m * k * 2 + b * k * 2 + b * m * 2
+
+
+def run_fp16_reference(args, torch, dev, peak: float) -> dict:
+    """µs per call of cuBLAS fp16 (torch.mv / torch.mm) and F.linear over a
+    chain of distinct fp16 weights (> 3x L2, CUDA graph, back to back) and
+    isolated (512 MiB flush, one call), per FP16_SHAPES entry.  A failure
+    here is reported in the key and does not end the run."""
+    import torch.nn.functional as F
+
+    steps = max(20, min(args.steps, 500))
+    out = []
+    try:
+        for m, k, b in FP16_SHAPES:
+            per = fp16_bytes(m, k, b)
+            nsets = max(4, -(-3 * L2_BYTES // per))
+            g = torch.Generator(device=dev).manual_seed(40000 + m + k + b)
+            ws = [(torch.randn(m, k, generator=g, device=dev) * 0.02).half()
+                  for _ in range(nsets)]
+            xs = [torch.randn(b, k, generator=g, device=dev).half() for _ in range(nsets)]
+            row = {"M": m, "K": k, "B": b, "sets": nsets, "bytes": per}
+            impls = {
+                ("cublas_fp16_gemv" if b == 1 else "cublas_fp16_gemm"):
+                    (lambda w, x: torch.mv(w, x[0])) if b == 1 else
+                    (lambda w, x: torch.mm(x, w.t())),
+                "pytorch_linear_fp16": lambda w, x: F.linear(x, w),
+            }
+            for name, fn in impls.items():
+                def step():
+                    for w, x in zip(ws, xs):
+                        fn(w, x)
+
+                step()
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step()
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (steps * nsets)
+                del graph
+                iso = time_isolated(torch, lambda: fn(ws[0], xs[0]), iters=100, warmup=10)
+                row[name] = {"us": us, "GBps": per / us / 1e3, "frac": per / us / 1e3 / peak,
+                             "isolated_us": iso}
+            out.append(row)
+            del ws, xs
+            torch.cuda.empty_cache()
+    except Exception as e:  # a reference point only: keep the run's line
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        return {"error": f"{type(e).__name__}: {e}"[:300], "shapes": out}
+    return {"protocol": f"fp16 weights (not W4): chain of {steps} replays of a CUDA graph of one "
+                        f"call per distinct weight (> 3x L2); isolated: 512 MiB fill flush, one "
+                        f"call, median of 100; bytes = fp16 W + x + y",
+            "shapes": out}
+
+
 def run_sweeps(args, torch, capi, quantize, dev, packed, scales, peak: float) -> dict:
     """Per-shape and per-batch lines for the BASELINE configs besides the
     headline: µs per GEMV in the chain (``value``'s protocol) and isolated
@@ -688,7 +764,8 @@ def run_sweeps(args, torch, capi, quantize, dev, packed, scales, peak: float) ->
     return {"protocol": f"chain: {steps} replays of a CUDA graph of one GEMV per distinct weight "
                         f"set (> 3x L2 of weights, PDL); isolated: 512 MiB fill flush, events "
                         f"around one plain C-ABI call, median of 100",
-            "shapes": shapes, "batch_sweep_4096x4096": batches}
+            "shapes": shapes, "batch_sweep_4096x4096": batches,
+            "cublas_fp16": run_fp16_reference(args, torch, dev, peak)}
 
 
 def tp_leg(args, workload: str, ws: int, rank: int, dev, dist, steps: int,

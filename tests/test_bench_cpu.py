@@ -79,6 +79,18 @@ def test_kernel_path_follows_the_dispatch():
     assert bench.kernel_path(28672, 8192, 32) == "k_batch (tcgen05)"
 
 
+def test_fp16_reference_bytes_are_the_references():
+    # The cross-precision cuBLAS points count fp16 W + x + y, as the
+    # reference's bytes_moved_fp16 does; the W4 metric counts packed W and
+    # scales instead.
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    assert bench.fp16_bytes(4096, 4096, 1) == 4096 * 4096 * 2 + 4096 * 2 + 4096 * 2
+    assert bench.fp16_bytes(11008, 4096, 8) == 11008 * 4096 * 2 + 8 * 4096 * 2 + 8 * 11008 * 2
+    assert (4096, 4096, 1) in bench.FP16_SHAPES  # (M, K, B)
+
+
 def test_run_meta_never_raises_without_a_gpu():
     sys.path.insert(0, str(REPO))
     import bench
